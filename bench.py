@@ -1,0 +1,416 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 quantized linear layer (one JSON line on rank 0).
+
+Workload (the decode sweep the metric is quoted on):
+  one *step* = the W4A16 GEMMs of one 27B decoder layer -- QKV (K=5120,N=7168),
+  O (5120,5120), gate_up (5120,34816), down (17408,5120) -- at every
+  M in {1,2,4,8,16}: 20 GEMMs, int4 group-128 weights, fp16 activations ~N(0,1),
+  fp16 scales ~U(0.005,0.02), fp16 out, fp32 accumulate.  Synthetic seeded data.
+  value = weight bytes streamed per step (int4 codes + fp16 scales) / step time.
+With --gpus N > 1 (torchrun, one rank per GPU) the same sweep runs tensor-parallel
+(Megatron): QKV and gate_up split by columns, O and down split by rows on
+group boundaries with an NCCL all-reduce of the fp16 output after each; value is
+the whole layer's weight bytes per step / max-over-ranks step time.
+
+--impl reference times the reference's algorithm on the host cores: the CPU
+restatement in oracle/ (the reference has no CPU GEMM of its own), same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816), ("down", 17408, 5120)]
+MS = [1, 2, 4, 8, 16]
+GROUP = 128
+METRIC = "W4A16 GEMM weight TB/s (M≤16) & TFLOPS (M≥1024) at 1–8 B200 vs roofline"
+
+
+def weight_bytes(K, N, wbits=4, group=GROUP):
+    return K * N * wbits // 8 + (K // group) * N * 2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU (oracle)
+
+class CpuSweep:
+    """The decode sweep on the host cores through the oracle's dequant-then-matmul."""
+
+    def __init__(self, nthreads: int):
+        import numpy as np
+        from oracle import oracle as o
+        self.o, self.nthreads = o, nthreads
+        rng = np.random.default_rng(0)
+        self.data = []
+        for name, K, N in SHAPES:
+            lin = rng.integers(0, 2**32, size=(K // 8, N), dtype=np.uint32)
+            S = o.round_to(rng.uniform(0.005, 0.02, size=(K // GROUP, N)).astype(np.float32), "f16")
+            As = {M: o.round_to(rng.standard_normal((M, K), dtype=np.float32), "f16") for M in MS}
+            self.data.append((K, N, lin, S, As))
+        self.bytes_per_pass = sum(weight_bytes(K, N) for _, K, N in SHAPES) * len(MS)
+
+    def one_pass(self):
+        for K, N, lin, S, As in self.data:
+            for M in MS:
+                self.o.w4_gemm(As[M], lin, S, group=GROUP, nthreads=self.nthreads)
+
+    def run(self, seconds: float):
+        """Passes until >= seconds elapsed (at least one); returns (TB/s, seconds, passes)."""
+        t0 = time.perf_counter()
+        passes = 0
+        while True:
+            self.one_pass()
+            passes += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                return self.bytes_per_pass * passes / el / 1e12, el, passes
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    sweep = CpuSweep(nthreads)
+    for _ in range(args.warmup):
+        sweep.one_pass()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sweep.one_pass()
+    step_s = (time.perf_counter() - t0) / args.steps
+    value = sweep.bytes_per_pass / step_s / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u4", "data": "synthetic",
+            "config": {"workload": "decode_sweep (BASELINE configs[1]): 27B layer QKV/O/gate_up/down x M in "
+                                   "{1,2,4,8,16}, int4 g128, fp16 A/scales", "parallelism": "host cores"},
+            "cpu_baseline": {"value": value, "unit": "TB/s", "cores": nthreads, "kind": "port",
+                             "sample": "one full pass of the decode sweep (20 GEMMs) per step: the oracle's "
+                                       "dequant-then-matmul (fp32, OpenMP) on all host threads"},
+            "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="hq", choices=["hq", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--copies", type=int, default=2, help="rotating weight copies per shape (defeats L2)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    from nebula_b200 import _lib, hq
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    peaks = load_peaks()
+    L = _lib.lib()
+
+    # ------------------------------------------------------------ workload
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    gemms = []  # (name, M, K_local, N_local, allreduce)
+    for M in MS:
+        for name, K, N in SHAPES:
+            if name in ("qkv", "gate_up"):
+                gemms.append((name, M, K, N // world, False))
+            else:
+                gemms.append((name, M, K // world, N, world > 1))
+    weights = {}
+    for name, K, N in SHAPES:
+        Kl, Nl = (K, N // world) if name in ("qkv", "gate_up") else (K // world, N)
+        copies = []
+        for c in range(args.copies):
+            W = torch.randint(0, 256, (hq.weight_bytes(_lib.HQ_WFMT_TILE_U4, Kl, Nl),), dtype=torch.uint8,
+                              device=dev, generator=g)
+            S = (torch.rand((Kl // GROUP, Nl), device=dev, generator=g) * 0.015 + 0.005).half()
+            copies.append((W, S))
+        weights[name] = (Kl, Nl, copies)
+    max_ws = max(int(L.hq_gemm_workspace_size(16, Nl, Kl, GROUP, _lib.HQ_WFMT_TILE_U4))
+                 for Kl, Nl, _ in weights.values())
+    ws = torch.zeros(max_ws, dtype=torch.uint8, device=dev)
+    acts = {M: {name: torch.randn((M, weights[name][0]), device=dev, generator=g).half() for name, _, _ in SHAPES}
+            for M in MS}
+    outs = {M: {name: torch.empty((M, weights[name][1]), device=dev, dtype=torch.float16) for name, _, _ in SHAPES}
+            for M in MS}
+
+    import ctypes
+    vp = ctypes.c_void_p
+
+    def launch(name, M, copy, stream_handle, A=None, C=None):
+        Kl, Nl, copies = weights[name]
+        W, S = copies[copy]
+        A = acts[M][name] if A is None else A
+        C = outs[M][name] if C is None else C
+        st = L.hq_gemm(vp(A.data_ptr()), _lib.HQ_F16, vp(W.data_ptr()), _lib.HQ_WFMT_TILE_U4, vp(S.data_ptr()),
+                       _lib.HQ_F16, None, vp(C.data_ptr()), _lib.HQ_F16, M, Nl, Kl, GROUP, vp(ws.data_ptr()),
+                       ws.numel(), vp(stream_handle))
+        if st != 0:
+            raise RuntimeError(L.hq_last_error_string().decode())
+        return C
+
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+
+    def step(copy, timing_events=None):
+        for i, (name, M, Kl, Nl, ar) in enumerate(gemms):
+            if timing_events is not None:
+                timing_events[i][0].record(stream)
+            C = launch(name, M, copy, sh)
+            if timing_events is not None:
+                timing_events[i][1].record(stream)
+            if ar:
+                dist.all_reduce(C)
+
+    # warm-up (also sets kernel attributes before graph capture)
+    with torch.cuda.stream(stream):
+        for w in range(args.warmup):
+            step(w % args.copies)
+    torch.cuda.synchronize()
+
+    # Capture one graph per weight copy: a step replays one graph.
+    graphs = []
+    for c in range(args.copies):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step(c)
+        graphs.append(gr)
+    for c in range(args.copies):
+        graphs[c].replay()
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------- timed region
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        ev0.record(stream)
+        for s in range(args.steps):
+            with torch.cuda.stream(stream):
+                graphs[s % args.copies].replay()
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    layer_bytes = sum(weight_bytes(K, N) for _, K, N in SHAPES)
+    step_bytes = layer_bytes * len(MS)
+    value = step_bytes / (ms / 1e3) / 1e12
+
+    # ----------------------------------------------- per-launch kernel timing
+    # Every GEMM of a step bracketed by events on its stream (no graph, no
+    # collectives): the decode kernel's average launch duration per shape.
+    per = []
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in gemms]
+    reps = max(3, min(args.steps, 10))
+    acc_ms = [0.0] * len(gemms)
+    with torch.cuda.stream(stream):
+        for r in range(reps):
+            for i, (name, M, Kl, Nl, ar) in enumerate(gemms):
+                evs[i][0].record(stream)
+                launch(name, M, r % args.copies, sh)
+                evs[i][1].record(stream)
+            torch.cuda.synchronize()
+            for i in range(len(gemms)):
+                acc_ms[i] += evs[i][0].elapsed_time(evs[i][1])
+    for i, (name, M, Kl, Nl, ar) in enumerate(gemms):
+        d = acc_ms[i] / reps
+        b = weight_bytes(Kl, Nl)
+        per.append({"shape": name, "M": M, "K": Kl, "N": Nl, "us": round(d * 1e3, 2),
+                    "GBps": round(b / (d / 1e3) / 1e9, 1)})
+    kern_bytes = sum(weight_bytes(Kl, Nl) for (_, _, Kl, Nl, _) in gemms)
+    kern_s = sum(acc_ms) / reps / 1e3
+    achieved = kern_bytes / kern_s / 1e9
+
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("traffic_ratio")
+        except (ValueError, OSError):
+            traffic = None
+
+    # ------------------------------------------------------------- e2e leg
+    # Public API with host buffers: pinned host A -> device, hq_gemm, C -> pinned host.
+    hostA = {M: {n: acts[M][n].cpu().pin_memory() for n, _, _ in SHAPES} for M in MS}
+    hostC = {M: {n: torch.empty_like(outs[M][n], device="cpu").pin_memory() for n, _, _ in SHAPES} for M in MS}
+    h2d = sum(hostA[M][n].numel() * 2 for (n, M, _, _, _) in gemms)
+    d2h = sum(hostC[M][n].numel() * 2 for (n, M, _, _, _) in gemms)
+
+    def e2e_step(copy):
+        for (name, M, Kl, Nl, ar) in gemms:
+            acts[M][name].copy_(hostA[M][name], non_blocking=True)
+            C = launch(name, M, copy, sh)
+            if ar:
+                dist.all_reduce(C)
+            hostC[M][name].copy_(C, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for w in range(3):
+            e2e_step(w % args.copies)
+    e2e_graphs = []
+    for c in range(args.copies):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            e2e_step(c)
+        e2e_graphs.append(gr)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        with torch.cuda.stream(stream):
+            e2e_graphs[s % args.copies].replay()
+    e1.record(stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = step_bytes / (e2e_ms / 1e3) / 1e12
+
+    hq.check_device_error()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nth = os.cpu_count() or 1
+        v, el, passes = CpuSweep(nth).run(args.cpu_seconds)
+        cpu = {"value": v, "unit": "TB/s", "cores": nth, "kind": "port",
+               "sample": f"{passes} full pass(es) of the decode sweep (20 GEMMs) in {el:.1f} s: oracle "
+                         "dequant-then-matmul, fp32 OpenMP, all host threads"}
+
+    for gr in graphs + e2e_graphs:
+        del gr
+    graphs.clear()
+    e2e_graphs.clear()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u4", "data": "synthetic (seeded random int4 codes, fp16 A ~N(0,1), "
+                                                         "fp16 scales ~U(0.005,0.02))",
+            "config": {"workload": "decode_sweep (BASELINE configs[1]): 27B layer QKV 5120x7168, O 5120x5120, "
+                                   "gate_up 5120x34816, down 17408x5120 at M in {1,2,4,8,16}; int4 g128, fp16 A",
+                       "global_batch": "M in {1,2,4,8,16}", "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": f"inputs larger than L2: {args.copies} rotating weight copies per shape "
+                             f"({args.copies * layer_bytes / 1e6:.0f} MB)",
+                       "graph": "each step is one CUDA graph replay"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": peaks["source"], "frac_of_nominal_8000": achieved / 8000.0,
+                         "kernel": "hq decode_kernel (bulk-copy ring + mma.sync dequant)",
+                         "algorithmic_bytes_per_step": kern_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": len(gemms) * args.steps,
+            "clocks": clocks.summary(),
+            "per_gemm": per,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,190 @@
+/*
+ * hq.h -- C ABI of the B200 (sm_100a) quantized-linear library (libhq.so).
+ *
+ * Drop-in replacement for the quantized linear layer of the hydrogen engine:
+ * int4 (W4A16) and ternary packed weights times fp16/bf16 activations with
+ * fp32 accumulation.  Every entry point is plain C: device pointers, sizes,
+ * enums and a CUDA stream handle; no exceptions cross this boundary.
+ *
+ * Reference interfaces replaced (paths inside the Nebula project):
+ *   hydrogen/include/marlin_gemm.hpp:59-172   hydrogen::MarlinGemmEngine
+ *   hydrogen/src/model/marlin_gemm.cu:432-467 repack_q4k_to_marlin (host repack)
+ *   hydrogen/src/model/marlin_gemm.cu:556-601 forward_marlin_int4 (the GEMM launch)
+ *   hydrogen/src/model/native_decoder.cu:155-206 kernel_gemv_tq1_0 (ternary GEMV)
+ * The reference has no C ABI for this path (its Rust crate
+ * crates/nebula-hydrogen exports IPC types only); these functions are additive.
+ *
+ * Conventions
+ *   - All tensor arguments are device pointers unless the name says host.
+ *   - Row-major: A is [M][K] (lda = K), C is [M][N] (ldc = N), scales and
+ *     biases are [K/group][N] (marlin_gemm.hpp:161-162).
+ *   - Calls are asynchronous on `stream`, stream-ordered, allocate nothing,
+ *     and may run concurrently on different streams with different
+ *     workspaces.  C is overwritten.
+ *   - Shapes: N % 16 == 0, K % 64 == 0, group % 64 == 0, K % group == 0
+ *     (the reference needs K % 512 == 0 and group % 32 == 0: marlin_gemm.cu
+ *     :156-159, so every reference shape with group >= 64 is accepted).
+ */
+#ifndef HQ_H
+#define HQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define HQ_API __declspec(dllexport)
+#else
+#define HQ_API __attribute__((visibility("default")))
+#endif
+
+/* Same object as cudaStream_t; declared here so callers need no CUDA headers. */
+typedef struct CUstream_st* hq_stream_t;
+
+typedef enum hq_status {
+    HQ_OK = 0,
+    HQ_ERR_INVALID_ARG = 1,       /* null pointer, bad enum, negative size */
+    HQ_ERR_UNSUPPORTED_SHAPE = 2, /* shape outside the rules above */
+    HQ_ERR_WORKSPACE_TOO_SMALL = 3,
+    HQ_ERR_CUDA = 4,              /* a CUDA runtime call failed; see hq_last_error_string */
+    HQ_ERR_TIMEOUT = 5,           /* a bounded device-side wait gave up */
+    HQ_ERR_MISALIGNED = 6,        /* a pointer breaks the 16-byte alignment rule */
+    HQ_ERR_UNSUPPORTED_DEVICE = 7 /* not an sm_100 device */
+} hq_status;
+
+typedef enum hq_dtype { HQ_F32 = 0, HQ_F16 = 1, HQ_BF16 = 2 } hq_dtype;
+
+typedef enum hq_wfmt {
+    /* uint32 [K/8][N]; word (kw,n) holds k = 8kw+i at bits 4i, code u = q+8.
+     * marlin_gemm.cu:495-510 (the reference's "linear" layout). */
+    HQ_WFMT_LINEAR_U4 = 0,
+    /* uint4 [K/32][N]; quad (kq,n) word j = linear word (4kq+j, n).
+     * marlin_gemm.cu:446-455 (the reference's "Marlin" layout). */
+    HQ_WFMT_MARLIN_QUAD = 1,
+    /* This library's tile order for int4: 16 columns x 64 k chunks of 512
+     * bytes, each lane's 16 bytes ready for one register dequant; strip
+     * groups of 128 columns contiguous along k.  Produced by hq_repack_*. */
+    HQ_WFMT_TILE_U4 = 2,
+    /* uint32 [K/16][N]; word (kw,n) holds k = 16kw+i at bits 2i, code t+1. */
+    HQ_WFMT_LINEAR_T2 = 3,
+    /* Tile order for 2-bit ternary (256-byte chunks). */
+    HQ_WFMT_TILE_T2 = 4,
+    /* [N][K/256] blocks of 56 bytes {fp16 d; u8 packed[52]; u16 pad}
+     * (native_decoder.cu:32-36). */
+    HQ_WFMT_TQ1_0 = 5
+} hq_wfmt;
+
+/* Library version string, e.g. "hq 0.1.0 sm_100a". */
+HQ_API const char* hq_version(void);
+
+/* Message for the most recent failing call on this host thread. */
+HQ_API const char* hq_last_error_string(void);
+
+/* Bytes of a packed weight tensor in `fmt` (0 if the shape is invalid). */
+HQ_API size_t hq_weight_bytes(hq_wfmt fmt, int K, int N);
+
+/* Workspace bytes that hq_gemm needs for this problem (a multiple of 256).
+ * The workspace holds split-K partial sums and per-strip-group arrival
+ * counters.  It must be zero-filled once before first use (hq_workspace_init);
+ * every call leaves the counters at zero again, so no per-call memset. */
+HQ_API size_t hq_gemm_workspace_size(int M, int N, int K, int group, hq_wfmt wfmt);
+HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t stream);
+
+/*
+ * The quantized linear layer:  C[M][N] = A[M][K] * dequant(Wq)   (fp32 accumulate)
+ *   dequant: int4   w = (u - 8) * scale[g][n]            (bias == NULL)
+ *                   w = u * scale[g][n] + bias[g][n]     (bias != NULL; reference
+ *                                                          form, marlin_gemm.cu:208-209)
+ *            ternary w = t * scale[g][n]
+ *   a_dtype: HQ_F16 | HQ_BF16 | HQ_F32 (f32 activations are split into two fp16
+ *            terms on chip, so the product keeps ~fp32 accuracy)
+ *   s_dtype: HQ_F16 | HQ_BF16 | HQ_F32; bias is always f32
+ *   c_dtype: HQ_F16 | HQ_BF16 | HQ_F32
+ *   wfmt:    HQ_WFMT_TILE_U4 / HQ_WFMT_TILE_T2 run directly.  LINEAR_U4,
+ *            MARLIN_QUAD and LINEAR_T2 are accepted for drop-in use and are
+ *            re-tiled into the workspace first (one extra pass over the
+ *            weights); hq_gemm_workspace_size accounts for it.
+ * M <= 16 runs the HBM-streaming decode kernel; larger M runs the tcgen05
+ * tensor-core kernel.
+ * Replaces MarlinGemmEngine::forward_marlin_int4 (marlin_gemm.cu:556-601).
+ */
+HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype,
+                         const void* Wq, hq_wfmt wfmt,
+                         const void* scales, hq_dtype s_dtype,
+                         const float* bias,
+                         void* C, hq_dtype c_dtype,
+                         int M, int N, int K, int group,
+                         void* workspace, size_t ws_bytes,
+                         hq_stream_t stream);
+
+/*
+ * Weight repack between formats, bit-exact in both directions.
+ * Supported (src -> dst): LINEAR_U4 -> MARLIN_QUAD (the reference repack,
+ * marlin_gemm.cu:432-467), MARLIN_QUAD -> LINEAR_U4, LINEAR_U4 -> TILE_U4,
+ * MARLIN_QUAD -> TILE_U4, TILE_U4 -> LINEAR_U4, LINEAR_T2 -> TILE_T2,
+ * TILE_T2 -> LINEAR_T2.
+ * hq_repack_host takes host pointers and runs synchronously on host threads
+ * (replaces MarlinGemmEngine::repack_q4k_to_marlin, marlin_gemm.hpp:78-83);
+ * hq_repack_device takes device pointers and runs on `stream`.
+ */
+HQ_API hq_status hq_repack_host(const void* src, hq_wfmt src_fmt, void* dst, hq_wfmt dst_fmt,
+                                int K, int N, int nthreads);
+HQ_API hq_status hq_repack_device(const void* src, hq_wfmt src_fmt, void* dst, hq_wfmt dst_fmt,
+                                  int K, int N, hq_stream_t stream);
+
+/*
+ * TQ1_0 matrix-vector product in the reference's own layout:
+ *   out[row] = sum_b sum_j d_b * trit_j * x[256b + j]; blocks with NaN/Inf d
+ *   are skipped.  x, out fp32; w = [out_dim][in_dim/256] TQ1_0 blocks.
+ * Replaces kernel_gemv_tq1_0 (native_decoder.cu:155-206), computing every row.
+ */
+HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
+                               int in_dim, int out_dim, hq_stream_t stream);
+
+/*
+ * Offline conversion of TQ1_0 weights ([N][K/256] blocks) into TILE_T2 codes
+ * plus fp16 group-128 scales [K/128][N] (the block scale repeated for both
+ * halves; a NaN/Inf block scale becomes 0, matching the reference's skip).
+ */
+HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
+                                     int K, int N, hq_stream_t stream);
+
+/*
+ * Device-side error word: kernels that wait on barriers give up after a
+ * bounded time and record a code here instead of hanging.  Synchronises the
+ * current device, returns HQ_ERR_TIMEOUT (and clears the word) if any kernel
+ * recorded a timeout since the last call, else HQ_OK.
+ */
+HQ_API hq_status hq_check_device_error(void);
+
+/*
+ * C wrappers of the drop-in hydrogen::MarlinGemmEngine shim
+ * (include/hq_marlin_gemm.hpp), for callers without C++.
+ * Same arguments and meaning as marlin_gemm.hpp:61, :78-83, :88-95, :100-107,
+ * :123-128, :133-139.  Return HQ_OK or an error code instead of throwing.
+ */
+typedef struct hq_marlin_engine hq_marlin_engine;
+HQ_API hq_marlin_engine* hq_marlin_engine_create(uint32_t M, uint32_t K, uint32_t N, uint32_t group_size);
+HQ_API void hq_marlin_engine_destroy(hq_marlin_engine* e);
+HQ_API hq_status hq_marlin_repack_q4k_to_marlin(hq_marlin_engine* e, const uint8_t* h_src_q4k,
+                                                uint32_t* h_dst_marlin, uint32_t K, uint32_t N,
+                                                double* repack_ms);
+HQ_API hq_status hq_marlin_forward_marlin_int4(hq_marlin_engine* e, const float* d_X,
+                                               const uint32_t* d_W_marlin, const float* d_scales,
+                                               const float* d_biases, float* d_Y, uint32_t M);
+HQ_API hq_status hq_marlin_forward_baseline_int4(hq_marlin_engine* e, const float* d_X,
+                                                 const uint32_t* d_W_linear, const float* d_scales,
+                                                 const float* d_biases, float* d_Y, uint32_t M);
+HQ_API hq_status hq_marlin_forward_reference(hq_marlin_engine* e, const float* d_X,
+                                             const float* d_W_dequant, float* d_Y_ref, uint32_t M);
+HQ_API hq_status hq_marlin_verify_fidelity(hq_marlin_engine* e, const float* d_Y_ref,
+                                           const float* d_Y_marlin, uint32_t M,
+                                           double* max_abs_err, double* mse);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HQ_H */

@@ -1,0 +1,258 @@
+// hq_common.cuh -- shared device helpers for the sm_100a quantized-linear kernels:
+// mbarrier / bulk-copy / tcgen05 / mma.sync wrappers (inline PTX), the fused
+// int4 and ternary register dequantisers, bounded waits and the device error word.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hq {
+
+// ------------------------------------------------------------------ errors
+// Kernels never spin forever: a wait that exceeds kWaitBudgetNs records a code
+// in the device error word (a __device__ variable of hq_api.cu whose address
+// every launch passes in) and the kernel winds down.  Read and cleared by
+// hq_check_device_error().
+enum DevError : unsigned { kDevOk = 0, kDevTimeout = 1 };
+
+constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void record_error(unsigned* err, unsigned code) {
+    if (err) atomicExch(err, code);
+}
+
+// ----------------------------------------------------------------- address
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true on success, false (and the device error word set) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            record_error(err, kDevTimeout);
+            return false;
+        }
+    }
+}
+
+// --------------------------------------------------------------- bulk copy
+// 1-D bulk copy global -> shared (TMA engine), completion via mbarrier tx bytes.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s_evict_first(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                                     uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Named barrier over a subset of warps (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------------ loads
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Read-only 16-byte load through L1 (activations: small, reused by every warp).
+__device__ __forceinline__ uint4 ldg128_nc(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// ---------------------------------------------------------------- lop3/prmt
+template <uint32_t LUT>
+__device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+    return d;
+}
+// (a & b) | c
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    return lop3<(0xF0 & 0xCC) | 0xAA>(a, b, c);
+}
+
+// ---------------------------------------------------------------- types
+template <typename T>
+struct TypeTraits;
+template <>
+struct TypeTraits<__half> {
+    static constexpr bool is_bf16 = false;
+};
+template <>
+struct TypeTraits<__nv_bfloat16> {
+    static constexpr bool is_bf16 = true;
+};
+
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+// --------------------------------------------------------------- dequant
+// Code fields are placed so that codes of k and k+1 sit 16 bits apart (see the
+// tile layout in hq_layout.h).  OR-ing a field into the mantissa of a
+// floating-point constant yields (constant + code) exactly; one more packed
+// subtract removes the constant and the code offset.  The result is the exact
+// small integer q (int4: -8..7, ternary: -1..1) in both halves.
+
+// int4 -> 4 x half2 holding (q[k0],q[k1]) (q[k2],q[k3]) (q[k4],q[k5]) (q[k6],q[k7]).
+// With `unsigned_codes` the raw code u = q + 8 is produced instead.
+template <bool kUnsigned = false>
+__device__ __forceinline__ void dequant_u4_f16(uint32_t w, uint32_t (&o)[4]) {
+    const uint32_t kMagic = 0x64006400u;          // 1024.0 in both halves
+    const uint32_t kSubLo = kUnsigned ? 0x64006400u : 0x64086408u;   // 1024 (+8)
+    const uint32_t kMulHi = 0x2C002C00u;          // 1/16
+    const uint32_t kAddHi = kUnsigned ? 0xD400D400u : 0xD480D480u;   // -64 (-72)
+    const uint32_t w8 = w >> 8;
+    uint32_t lo0 = and_or(w, 0x000F000Fu, kMagic);
+    uint32_t hi0 = and_or(w, 0x00F000F0u, kMagic);
+    uint32_t lo1 = and_or(w8, 0x000F000Fu, kMagic);
+    uint32_t hi1 = and_or(w8, 0x00F000F0u, kMagic);
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(lo0), "r"(kSubLo));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[1]) : "r"(hi0), "r"(kMulHi), "r"(kAddHi));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(lo1), "r"(kSubLo));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[3]) : "r"(hi1), "r"(kMulHi), "r"(kAddHi));
+}
+
+template <bool kUnsigned = false>
+__device__ __forceinline__ void dequant_u4_bf16(uint32_t w, uint32_t (&o)[4]) {
+    const uint32_t kMagic = 0x43004300u;                             // 128.0
+    const uint32_t kSub = kUnsigned ? 0x43004300u : 0x43084308u;     // 128 (+8)
+    uint32_t a0 = and_or(w, 0x000F000Fu, kMagic);
+    uint32_t a1 = and_or(w >> 4, 0x000F000Fu, kMagic);
+    uint32_t a2 = and_or(w >> 8, 0x000F000Fu, kMagic);
+    uint32_t a3 = and_or(w >> 12, 0x000F000Fu, kMagic);
+    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(a0), "r"(kSub));
+    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(a1), "r"(kSub));
+    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(a2), "r"(kSub));
+    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[3]) : "r"(a3), "r"(kSub));
+}
+
+// ternary: pair p (codes of k=2p, 2p+1) sits at bits (2p, 16+2p).
+template <bool kBF16>
+__device__ __forceinline__ uint32_t dequant_t2_pair(uint32_t w, int p) {
+    const uint32_t kMagic = kBF16 ? 0x43004300u : 0x64006400u;
+    const uint32_t kSub = kBF16 ? 0x43014301u : 0x64016401u;  // constant + 1
+    uint32_t a = and_or(w >> (2 * p), 0x00030003u, kMagic);
+    uint32_t o;
+    if (kBF16)
+        asm("sub.bf16x2 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(kSub));
+    else
+        asm("sub.f16x2 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(kSub));
+    return o;
+}
+
+// ------------------------------------------------------------- mma.sync
+// D(16x8,f32) += A(16x16) * B(16x8), fp16 or bf16 inputs.
+template <bool kBF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if (kBF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+}
+
+}  // namespace hq

@@ -1,0 +1,73 @@
+// hq_internal.h -- internal (non-ABI) interfaces between the API layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace hq {
+
+enum class DType : int { F32 = 0, F16 = 1, BF16 = 2 };
+
+struct GemmArgs {
+    const void* A;
+    DType a_dtype;
+    const uint8_t* W;  // tile format
+    int wbits;         // 4 or 2
+    const void* S;
+    DType s_dtype;
+    const float* bias;  // nullable
+    void* C;
+    DType c_dtype;
+    int M, N, K, group;
+    uint8_t* ws;  // 256-byte aligned workspace (after any re-tiled weights)
+    size_t ws_bytes;
+    cudaStream_t stream;
+};
+
+struct DeviceInfo {
+    int sm_count;
+    int cc_major, cc_minor;
+    size_t smem_optin;
+};
+const DeviceInfo& device_info(int dev);
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
+cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes);
+
+// Decode (M <= 16) HBM-streaming kernel.
+size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev);
+bool decode_supported(const GemmArgs& a);
+cudaError_t launch_decode(const GemmArgs& a);
+
+// Tensor-core (tcgen05) kernel for larger M.
+size_t prefill_workspace_bytes(int M, int N, int K, int wbits, int dev);
+bool prefill_supported(const GemmArgs& a);
+cudaError_t launch_prefill(const GemmArgs& a);
+
+// Repack kernels (device).
+cudaError_t launch_linear_to_tile(const void* src, bool src_is_quad, int wbits, uint8_t* dst, int K, int N,
+                                  cudaStream_t s);
+cudaError_t launch_tile_to_linear(const uint8_t* src, int wbits, uint32_t* dst, int K, int N, cudaStream_t s);
+cudaError_t launch_linear_to_quad(const uint32_t* src, uint32_t* dst, int K, int N, bool inverse, cudaStream_t s);
+
+namespace host {
+void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, int K, int N, int nthreads);
+void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N, int nthreads);
+void linear_quad(const uint32_t* src, uint32_t* dst, int K, int N, bool inverse, int nthreads);
+}  // namespace host
+
+// TQ1_0 kernels.
+cudaError_t launch_tq1_0_gemv(const float* x, const uint8_t* w, float* out, int in_dim, int out_dim, cudaStream_t s);
+cudaError_t launch_tq1_0_to_tile_t2(const uint8_t* w, uint8_t* tile, uint16_t* scales, int K, int N, cudaStream_t s);
+
+// Plain fp32 GEMM (the engine shim's forward_reference).
+cudaError_t launch_f32_gemm(const float* X, const float* W, float* Y, int M, int K, int N, cudaStream_t s);
+
+// Message returned by hq_last_error_string() on this host thread.
+void set_last_error(const char* msg);
+
+// Device error word: address on device `dev` (passed to kernels), read+clear.
+unsigned* device_error_word(int dev);
+cudaError_t read_and_clear_device_error(unsigned* code);
+
+}  // namespace hq

@@ -1,0 +1,180 @@
+"""Python host side of the quantized linear layer (torch tensors in, libhq.so underneath).
+
+Mirrors the reference's operator interface for this path:
+  * ``MarlinGemmEngine`` -- the methods of hydrogen::MarlinGemmEngine
+    (hydrogen/include/marlin_gemm.hpp:59-172) with the same argument meaning
+    (device tensors for X / weights / scales / biases / Y, M rows), raising
+    ``HQError`` where the reference throws std::runtime_error;
+  * ``tq1_0_gemv`` -- kernel_gemv_tq1_0 (hydrogen/src/model/native_decoder.cu:155-206);
+  * ``QuantLinear`` / ``gemm`` -- the production entry (hq_gemm) on tile-order
+    weights produced once by ``repack``.
+All device work runs on the caller's current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (HQ_BF16, HQ_F16, HQ_F32, HQ_WFMT_LINEAR_T2, HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD,
+                   HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TQ1_0, HQError, check, lib)
+
+__all__ = ["HQError", "weight_bytes", "repack_host", "repack", "make_workspace", "gemm", "QuantLinear",
+           "tq1_0_gemv", "tq1_0_to_tile_t2", "check_device_error", "MarlinGemmEngine",
+           "HQ_WFMT_LINEAR_U4", "HQ_WFMT_MARLIN_QUAD", "HQ_WFMT_TILE_U4", "HQ_WFMT_LINEAR_T2",
+           "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0"]
+
+_DT = {torch.float32: HQ_F32, torch.float16: HQ_F16, torch.bfloat16: HQ_BF16}
+
+
+def _dt(t: torch.dtype) -> int:
+    try:
+        return _DT[t]
+    except KeyError:
+        raise HQError(_lib.HQ_ERR_INVALID_ARG, f"unsupported dtype {t}") from None
+
+
+def _stream(stream=None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t) -> ctypes.c_void_p | None:
+    if t is None:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def weight_bytes(fmt: int, K: int, N: int) -> int:
+    return int(lib().hq_weight_bytes(fmt, K, N))
+
+
+def repack_host(src: np.ndarray, src_fmt: int, dst_fmt: int, K: int, N: int, nthreads: int = 0) -> np.ndarray:
+    """Bit-exact host repack (hq_repack_host); returns a uint32 array in dst_fmt."""
+    src = np.ascontiguousarray(src)
+    nb = weight_bytes(dst_fmt, K, N)
+    if nb == 0:
+        raise HQError(_lib.HQ_ERR_UNSUPPORTED_SHAPE, f"no {dst_fmt} layout for K={K} N={N}")
+    dst = np.empty(nb // 4, np.uint32)
+    check(lib().hq_repack_host(src.ctypes.data_as(ctypes.c_void_p), src_fmt, dst.ctypes.data_as(ctypes.c_void_p),
+                               dst_fmt, K, N, nthreads))
+    return dst
+
+
+def repack(src: torch.Tensor, src_fmt: int, dst_fmt: int, K: int, N: int, stream=None) -> torch.Tensor:
+    """Bit-exact device repack (hq_repack_device) into a new uint8 tensor."""
+    nb = weight_bytes(dst_fmt, K, N)
+    if nb == 0:
+        raise HQError(_lib.HQ_ERR_UNSUPPORTED_SHAPE, f"no {dst_fmt} layout for K={K} N={N}")
+    dst = torch.empty(nb, dtype=torch.uint8, device=src.device)
+    check(lib().hq_repack_device(_ptr(src), src_fmt, _ptr(dst), dst_fmt, K, N, _stream(stream)))
+    return dst
+
+
+def make_workspace(M: int, N: int, K: int, group: int, wfmt: int, device) -> torch.Tensor:
+    """Zero-filled workspace for hq_gemm (split-K partials + self-resetting counters)."""
+    with torch.cuda.device(device):
+        nb = int(lib().hq_gemm_workspace_size(M, N, K, group, wfmt))
+    if nb == 0:
+        raise HQError(_lib.HQ_ERR_UNSUPPORTED_SHAPE, f"bad shape M={M} N={N} K={K} group={group}")
+    return torch.zeros(nb, dtype=torch.uint8, device=device)
+
+
+def gemm(A: torch.Tensor, W: torch.Tensor, scales: torch.Tensor, *, N: int, group: int = 128,
+         wfmt: int = HQ_WFMT_TILE_U4, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """C = A @ dequant(W) through hq_gemm.  A: [M, K] device tensor."""
+    M, K = A.shape
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
+    if workspace is None:
+        workspace = make_workspace(M, N, K, group, wfmt, A.device)
+    check(lib().hq_gemm(_ptr(A), _dt(A.dtype), _ptr(W), wfmt, _ptr(scales), _dt(scales.dtype), _ptr(bias),
+                        _ptr(out), _dt(out.dtype), M, N, K, group, _ptr(workspace), workspace.numel(),
+                        _stream(stream)))
+    return out
+
+
+class QuantLinear:
+    """A packed quantized linear layer: tile-order weights + group scales + workspace."""
+
+    def __init__(self, W_tile: torch.Tensor, scales: torch.Tensor, K: int, N: int, group: int = 128,
+                 wbits: int = 4, max_m: int = 16):
+        self.W, self.scales, self.K, self.N, self.group = W_tile, scales, K, N, group
+        self.wfmt = HQ_WFMT_TILE_U4 if wbits == 4 else HQ_WFMT_TILE_T2
+        self.max_m = max_m
+        self.workspace = make_workspace(max_m, N, K, group, self.wfmt, W_tile.device)
+
+    def __call__(self, A: torch.Tensor, out: torch.Tensor | None = None, out_dtype=None, stream=None):
+        if A.shape[0] > self.max_m:
+            self.max_m = A.shape[0]
+            self.workspace = make_workspace(self.max_m, self.N, self.K, self.group, self.wfmt, A.device)
+        return gemm(A, self.W, self.scales, N=self.N, group=self.group, wfmt=self.wfmt, out=out,
+                    out_dtype=out_dtype, workspace=self.workspace, stream=stream)
+
+
+def tq1_0_gemv(x: torch.Tensor, w: torch.Tensor, out_dim: int, out: torch.Tensor | None = None,
+               stream=None) -> torch.Tensor:
+    in_dim = x.numel()
+    if out is None:
+        out = torch.empty(out_dim, dtype=torch.float32, device=x.device)
+    check(lib().hq_tq1_0_gemv(_ptr(x), _ptr(w), _ptr(out), in_dim, out_dim, _stream(stream)))
+    return out
+
+
+def tq1_0_to_tile_t2(w: torch.Tensor, K: int, N: int, stream=None):
+    tile = torch.empty(weight_bytes(HQ_WFMT_TILE_T2, K, N), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((K // 128, N), dtype=torch.float16, device=w.device)
+    check(lib().hq_tq1_0_to_tile_t2(_ptr(w), _ptr(tile), _ptr(scales), K, N, _stream(stream)))
+    return tile, scales
+
+
+def check_device_error() -> None:
+    check(lib().hq_check_device_error())
+
+
+class MarlinGemmEngine:
+    """hydrogen::MarlinGemmEngine (marlin_gemm.hpp:59-172) through the C wrappers."""
+
+    def __init__(self, M: int, K: int, N: int, group_size: int = 128):
+        self._h = lib().hq_marlin_engine_create(M, K, N, group_size)
+        if not self._h:
+            raise HQError(_lib.HQ_ERR_CUDA, lib().hq_last_error_string().decode(errors="replace"))
+        self.M, self.K, self.N, self.group_size = M, K, N, group_size
+
+    def close(self):
+        if self._h:
+            lib().hq_marlin_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def repack_q4k_to_marlin(self, h_src: np.ndarray, K: int, N: int):
+        src = np.ascontiguousarray(h_src, dtype=np.uint32)
+        dst = np.zeros((K // 32, N, 4), np.uint32)
+        ms = ctypes.c_double(0)
+        check(lib().hq_marlin_repack_q4k_to_marlin(self._h, src.ctypes.data_as(ctypes.c_void_p),
+                                                   dst.ctypes.data_as(ctypes.c_void_p), K, N, ctypes.byref(ms)))
+        return dst, ms.value
+
+    def forward_marlin_int4(self, X, W_marlin, scales, biases, Y, M):
+        check(lib().hq_marlin_forward_marlin_int4(self._h, _ptr(X), _ptr(W_marlin), _ptr(scales), _ptr(biases),
+                                                  _ptr(Y), M))
+
+    def forward_baseline_int4(self, X, W_linear, scales, biases, Y, M):
+        check(lib().hq_marlin_forward_baseline_int4(self._h, _ptr(X), _ptr(W_linear), _ptr(scales),
+                                                    _ptr(biases), _ptr(Y), M))
+
+    def forward_reference(self, X, W_dequant, Y_ref, M):
+        check(lib().hq_marlin_forward_reference(self._h, _ptr(X), _ptr(W_dequant), _ptr(Y_ref), M))
+
+    def verify_fidelity(self, Y_ref, Y, M):
+        mx, mse = ctypes.c_double(0), ctypes.c_double(0)
+        check(lib().hq_marlin_verify_fidelity(self._h, _ptr(Y_ref), _ptr(Y), M, ctypes.byref(mx), ctypes.byref(mse)))
+        return mx.value, mse.value

@@ -1,0 +1,184 @@
+"""GPU parity of the decode (M <= 16) kernel, the repacks and the TQ1_0 path, all called
+through the C ABI (libhq.so) and checked against the CPU oracle.
+
+Tolerance (from the task statement): max|y - y_ref| / max|y_ref| <= 1e-2 for fp16
+and <= 2e-2 for bf16 against the fp32 oracle; integer/byte work (repacks) is
+compared bit for bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+from nebula_b200 import _lib, hq
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f16": 1e-2, "bf16": 2e-2, "f32": 1e-4}
+TDT = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+
+
+def cuda(x, dtype="f32"):
+    """Upload: float arrays converted to `dtype` (exact: values are representable); dtype None
+    uploads the raw bytes as uint8."""
+    x = np.ascontiguousarray(x)
+    if dtype is None:
+        return torch.from_numpy(x.view(np.uint8).reshape(-1)).to("cuda:0")
+    return torch.from_numpy(x.astype(np.float32)).to("cuda:0").to(TDT[dtype])
+
+
+def run_gemm(A, W_dev, S, N, group, dtype, wfmt=_lib.HQ_WFMT_TILE_U4, out_dtype=None, bias=None, s_dtype=None):
+    At = cuda(A, dtype)
+    St = cuda(S, s_dtype or dtype)
+    Bt = cuda(bias, "f32") if bias is not None else None
+    Y = hq.gemm(At, W_dev, St, N=N, group=group, wfmt=wfmt, bias=Bt, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return Y.float().cpu().numpy()
+
+
+SHAPES = [(256, 48, 128), (512, 144, 64), (384, 256, 128), (1024, 1040, 128), (5120, 5120, 128)]
+
+
+@pytest.mark.parametrize("K,N,g", SHAPES)
+@pytest.mark.parametrize("M", [1, 2, 3, 8, 9, 16])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_decode_int4_parity(K, N, g, M, dtype):
+    A, q, S = o.gen_int4_case(M, K, N, group=g, seed=M * 131 + K + N, a_dtype=dtype)
+    lin = o.pack_linear_u4(q)
+    ref = o.w4_gemm(A, lin, S, group=g)
+    W = cuda(o.pack_tile(q, 4), None)
+    y16 = run_gemm(A, W, S, N, g, dtype)
+    assert o.max_rel_err(y16, ref) <= TOL[dtype]
+    y32 = run_gemm(A, W, S, N, g, dtype, out_dtype=torch.float32)
+    assert o.max_rel_err(y32, ref) <= 1e-5  # fp32 output: only accumulation-order differences
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_reference_layouts_give_identical_results(M):
+    K, N, g = 1024, 272, 128
+    A, q, S = o.gen_int4_case(M, K, N, group=g, seed=99)
+    lin = o.pack_linear_u4(q)
+    quad = o.repack_marlin_quad(lin, K, N)
+    y_tile = run_gemm(A, cuda(o.pack_tile(q, 4), None), S, N, g, "f16")
+    y_lin = run_gemm(A, cuda(lin, None), S, N, g, "f16", wfmt=_lib.HQ_WFMT_LINEAR_U4)
+    y_quad = run_gemm(A, cuda(quad, None), S, N, g, "f16", wfmt=_lib.HQ_WFMT_MARLIN_QUAD)
+    assert np.array_equal(y_tile, y_lin) and np.array_equal(y_tile, y_quad)
+
+
+def test_decode_is_deterministic_and_leaves_counters_zero():
+    K, N, g, M = 17408, 5120, 128, 16
+    A, q, S = o.gen_int4_case(M, K, N, group=g, seed=5)
+    W = cuda(o.pack_tile(q, 4), None)
+    At, St = cuda(A, "f16"), cuda(S, "f16")
+    ws = hq.make_workspace(M, N, K, g, _lib.HQ_WFMT_TILE_U4, At.device)
+    y1 = hq.gemm(At, W, St, N=N, group=g, workspace=ws).clone()
+    y2 = hq.gemm(At, W, St, N=N, group=g, workspace=ws).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    nsg = (N // 16 + 7) // 8
+    assert int(ws[: nsg * 4].view(torch.int32).abs().sum()) == 0
+    ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=g)
+    assert o.max_rel_err(y1.float().cpu().numpy(), ref) <= TOL["f16"]
+    hq.check_device_error()
+
+
+@pytest.mark.parametrize("name,K,N", [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816),
+                                      ("down", 17408, 5120)])
+@pytest.mark.parametrize("M", [1, 16])
+def test_decode_27b_shapes(name, K, N, M):
+    """BASELINE config 1 shapes at full size (the oracle runs these in well under a second)."""
+    A, q, S = o.gen_int4_case(M, K, N, group=128, seed={"qkv": 1, "o": 2, "gate_up": 3, "down": 4}[name] * 100 + M, a_dtype="f16")
+    ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=128)
+    W = hq.repack(cuda(o.pack_linear_u4(q), None), _lib.HQ_WFMT_LINEAR_U4, _lib.HQ_WFMT_TILE_U4, K, N)
+    y = run_gemm(A, W, S, N, 128, "f16")
+    assert o.max_rel_err(y, ref) <= TOL["f16"]
+
+
+def test_config0_against_golden():
+    """BASELINE config 0 (A fp16 [16,4096], int4 [4096,4096] g128, seed 0) vs the committed oracle output."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+    A, q, S = o.gen_int4_case(16, 4096, 4096, group=128, seed=0, a_dtype="f16")
+    y = run_gemm(A, cuda(o.pack_tile(q, 4), None), S, 4096, 128, "f16")
+    assert o.max_rel_err(y, g["cfg0_Y"]) <= TOL["f16"]
+
+
+@pytest.mark.parametrize("K,N", [(256, 32), (512, 144), (5120, 7168)])
+@pytest.mark.parametrize("M", [1, 7, 16])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_decode_ternary_parity(K, N, M, dtype):
+    A, t, S = o.gen_ternary_case(M, K, N, group=128, seed=K + M, a_dtype=dtype)
+    ref = o.t2_gemm(A, o.pack_linear_t2(t), S, group=128)
+    W = cuda(o.pack_tile(t, 2), None)
+    y = run_gemm(A, W, S.astype(np.float32), N, 128, dtype, wfmt=_lib.HQ_WFMT_TILE_T2, s_dtype=dtype)
+    assert o.max_rel_err(y, ref) <= TOL[dtype]
+
+
+def test_f32_activations_with_bias_match_reference_semantics():
+    """The reference's own form: fp32 X, fp32 scale and bias, w = u*s + b (marlin_gemm.cu:208-209),
+    with its synthetic distributions (:470-487) and its acceptance bound max_abs_error < 1e-3."""
+    rng = np.random.default_rng(42)
+    M, K, N, g = 8, 4096, 4096, 128
+    X = (rng.standard_normal((M, K)) * 0.25).astype(np.float32)
+    S = (0.05 + rng.integers(0, 1000, size=(K // g, N)) * 1e-4).astype(np.float32)
+    B = (-8.0 * S).astype(np.float32)
+    q = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    lin = o.pack_linear_u4(q)
+    ref = o.w4_gemm(X, lin, S, B, group=g)
+    quad = o.repack_marlin_quad(lin, K, N)
+    y = run_gemm(X, cuda(quad, None), S, N, g, "f32", wfmt=_lib.HQ_WFMT_MARLIN_QUAD, bias=B)
+    assert np.max(np.abs(y - ref)) < 1e-3
+    y2 = run_gemm(X, cuda(quad, None), S, N, g, "f32", wfmt=_lib.HQ_WFMT_MARLIN_QUAD)  # symmetric form
+    ref2 = o.w4_gemm(X, lin, S, None, group=g)
+    assert np.max(np.abs(y2 - ref2)) < 1e-3
+
+
+@pytest.mark.parametrize("K,N", [(64, 16), (512, 144), (5120, 7168)])
+def test_device_repacks_bit_exact(K, N):
+    rng = np.random.default_rng(K + N)
+    q = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    lin = o.pack_linear_u4(q)
+    quad = o.repack_marlin_quad(lin, K, N)
+    tile = o.pack_tile(q, 4)
+    got = lambda src, sf, df: hq.repack(cuda(src, None), sf, df, K, N).cpu().numpy()  # noqa: E731
+    assert np.array_equal(got(lin, _lib.HQ_WFMT_LINEAR_U4, _lib.HQ_WFMT_TILE_U4), tile)
+    assert np.array_equal(got(quad, _lib.HQ_WFMT_MARLIN_QUAD, _lib.HQ_WFMT_TILE_U4), tile)
+    assert np.array_equal(got(tile, _lib.HQ_WFMT_TILE_U4, _lib.HQ_WFMT_LINEAR_U4).view(np.uint32), lin.ravel())
+    assert np.array_equal(got(lin, _lib.HQ_WFMT_LINEAR_U4, _lib.HQ_WFMT_MARLIN_QUAD).view(np.uint32), quad.ravel())
+    assert np.array_equal(got(quad, _lib.HQ_WFMT_MARLIN_QUAD, _lib.HQ_WFMT_LINEAR_U4).view(np.uint32), lin.ravel())
+    t = rng.integers(-1, 2, size=(K, N), dtype=np.int8)
+    lin2, tile2 = o.pack_linear_t2(t), o.pack_tile(t, 2)
+    assert np.array_equal(got(lin2, _lib.HQ_WFMT_LINEAR_T2, _lib.HQ_WFMT_TILE_T2), tile2)
+    assert np.array_equal(got(tile2, _lib.HQ_WFMT_TILE_T2, _lib.HQ_WFMT_LINEAR_T2).view(np.uint32), lin2.ravel())
+
+
+def test_tq1_0_gemv_golden_and_conversion():
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+    K, N, _ = (int(v) for v in g["tq1_meta"])
+    x, blob = cuda(g["tq1_x"], "f32"), cuda(g["tq1_blob"], None)
+    y = hq.tq1_0_gemv(x, blob, N)
+    torch.cuda.synchronize()
+    assert o.max_rel_err(y.cpu().numpy(), g["tq1_y"]) <= 1e-5
+    # offline conversion to the 2-bit tile order, then the decode kernel (fp16 activations)
+    tile, scales = hq.tq1_0_to_tile_t2(blob, K, N)
+    t_kn = np.ascontiguousarray(g["tq1_t"].T)
+    assert np.array_equal(tile.cpu().numpy(), o.pack_tile(t_kn, 2))
+    x16 = o.round_to(g["tq1_x"], "f16")
+    y2 = hq.gemm(cuda(x16[None, :], "f16"), tile, scales, N=N, group=128, wfmt=_lib.HQ_WFMT_TILE_T2,
+                 out_dtype=torch.float32)
+    ref2 = o.gemv_tq1_0(x16, g["tq1_blob"], K, N)
+    assert o.max_rel_err(y2.cpu().numpy()[0], ref2) <= TOL["f16"]
+
+
+@pytest.mark.parametrize("K,N", [(5120, 7168), (17408, 5120)])
+def test_tq1_0_gemv_full_size(K, N):
+    rng = np.random.default_rng(K)
+    t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+    blob = o.pack_tq1_0(t, d)
+    x = rng.standard_normal(K).astype(np.float32)
+    ref = o.gemv_tq1_0(x, blob, K, N)
+    y = hq.tq1_0_gemv(cuda(x, "f32"), cuda(blob, None), N)
+    torch.cuda.synchronize()
+    assert o.max_rel_err(y.cpu().numpy(), ref) <= 1e-5
