@@ -18,6 +18,7 @@
  *   - All tensor arguments are device pointers unless the name says host.
  *   - Row-major: A is [M][K] (lda = K), C is [M][N] (ldc = N), scales and
  *     biases are [K/group][N] (marlin_gemm.hpp:161-162).
+ *   - Device pointers handed to hq_gemm are 16-byte aligned.
  *   - Calls are asynchronous on `stream`, stream-ordered, allocate nothing,
  *     and may run concurrently on different streams with different
  *     workspaces.  C is overwritten.
@@ -86,10 +87,12 @@ HQ_API const char* hq_last_error_string(void);
 /* Bytes of a packed weight tensor in `fmt` (0 if the shape is invalid). */
 HQ_API size_t hq_weight_bytes(hq_wfmt fmt, int K, int N);
 
-/* Workspace bytes that hq_gemm needs for this problem (a multiple of 256).
- * The workspace holds split-K partial sums and per-strip-group arrival
- * counters.  It must be zero-filled once before first use (hq_workspace_init);
- * every call leaves the counters at zero again, so no per-call memset. */
+/* Workspace bytes that hq_gemm needs for this problem (a multiple of 256;
+ * 0 when none is needed, in which case workspace may be NULL).  The workspace
+ * holds re-tiled weights for the reference layouts and the tensor-core
+ * kernel's split-K state.  Zero-fill it once before first use
+ * (hq_workspace_init); calls leave any counters in it at zero again, so no
+ * per-call memset. */
 HQ_API size_t hq_gemm_workspace_size(int M, int N, int K, int group, hq_wfmt wfmt);
 HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t stream);
 
@@ -109,6 +112,13 @@ HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t
  *            weights); hq_gemm_workspace_size accounts for it.
  * M <= 16 runs the HBM-streaming decode kernel; larger M runs the tcgen05
  * tensor-core kernel.
+ * Launch overlap (on by default, see hq_set_launch_overlap): a call may start
+ * reading Wq and scales while the kernel enqueued just before it on the same
+ * stream is still running (programmatic dependent launch); A is read only
+ * after that kernel has finished.  Tile-order weights must therefore not be
+ * written by the immediately preceding kernel on the stream (weights loaded at
+ * start-up, as in the hydrogen engine, are fine); reference-layout weights
+ * (re-tiled inside the call) are never read early.
  * Replaces MarlinGemmEngine::forward_marlin_int4 (marlin_gemm.cu:556-601).
  */
 HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype,
@@ -151,6 +161,10 @@ HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
  */
 HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
                                      int K, int N, hq_stream_t stream);
+
+/* Turn the launch overlap described at hq_gemm on (1, default) or off (0)
+ * for the whole process. */
+HQ_API void hq_set_launch_overlap(int enable);
 
 /*
  * Device-side error word: kernels that wait on barriers give up after a

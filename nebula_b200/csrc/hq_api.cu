@@ -179,7 +179,7 @@ HQ_API size_t hq_gemm_workspace_size(int M, int N, int K, int group, hq_wfmt wfm
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
     size_t retile = fmt_is_tile(wfmt) ? 0 : up256(TileGeom(K, N, wbits).bytes());
-    return retile + kernel_ws(M, N, K, wbits, dev) + 256;
+    return retile + kernel_ws(M, N, K, wbits, dev);
 }
 
 HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t stream) {
@@ -199,14 +199,16 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype, const void* Wq, hq_wfm
     if (!wbits) return fail(HQ_ERR_INVALID_ARG, "unsupported weight format %d for hq_gemm", (int)wfmt);
     if (!valid_dtype(a_dtype) || !valid_dtype(s_dtype) || !valid_dtype(c_dtype))
         return fail(HQ_ERR_INVALID_ARG, "bad dtype enum");
-    if (!A || !Wq || !scales || !C || !workspace) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
-    if (!aligned16(A) || !aligned16(Wq) || !aligned16(C) || !aligned16(workspace))
-        return fail(HQ_ERR_MISALIGNED, "A, Wq, C and workspace must be 16-byte aligned");
+    if (!A || !Wq || !scales || !C) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(A) || !aligned16(Wq) || !aligned16(C) || !aligned16(workspace) || !aligned16(scales) ||
+        (bias && !aligned16(bias)))
+        return fail(HQ_ERR_MISALIGNED, "A, Wq, scales, bias, C and workspace must be 16-byte aligned");
     if (bias && wbits != 4) return fail(HQ_ERR_INVALID_ARG, "bias is only defined for int4 weights");
     int dev = 0;
     if ((st = check_device(&dev)) != HQ_OK) return st;
 
     const size_t need = hq_gemm_workspace_size(M, N, K, group, wfmt);
+    if (need && !workspace) return fail(HQ_ERR_INVALID_ARG, "null workspace (%zu bytes required)", need);
     if (ws_bytes < need) return fail(HQ_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -234,8 +236,9 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype, const void* Wq, hq_wfm
     a.N = N;
     a.K = K;
     a.group = group;
+    a.weights_just_written = !fmt_is_tile(wfmt);
     a.ws = ws;
-    a.ws_bytes = ws_bytes - (size_t)(ws - static_cast<uint8_t*>(workspace));
+    a.ws_bytes = workspace ? ws_bytes - (size_t)(ws - static_cast<uint8_t*>(workspace)) : 0;
     a.stream = s;
 
     if (M > 16) {
@@ -359,6 +362,8 @@ HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* sca
                                             reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "tq1_0 conversion launch");
 }
+
+HQ_API void hq_set_launch_overlap(int enable) { set_decode_launch_overlap(enable != 0); }
 
 HQ_API hq_status hq_check_device_error(void) {
     unsigned code = 0;

@@ -55,25 +55,34 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting warp is parked by the hardware
+// (for at most ~1 ms per call) instead of spinning on the issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
 
 // Bounded wait: true on success, false (and the device error word set) on timeout.
+// Between failed polls the thread sleeps with exponential backoff (32..kMaxNs ns)
+// so that waiting warps do not take issue slots from the working ones.
+template <unsigned kMaxNs = 256>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
+    unsigned ns = 32;
     while (true) {
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 8; ++i) {
+            __nanosleep(ns);
             if (mbar_try_wait(bar, parity)) return true;
+            ns = ns < kMaxNs ? 2 * ns : kMaxNs;
+        }
         if (globaltimer_ns() - t0 > kWaitBudgetNs) {
             record_error(err, kDevTimeout);
             return false;
@@ -101,6 +110,17 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void* smem_dst, const void*
         : "memory");
 }
 
+// 2-D tiled TMA load of box {x, y} (x innermost, in elements) from a tensor map
+// held in kernel parameter space; completion via mbarrier tx bytes.  x times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -112,6 +132,45 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+
+// ---------------------------------------------------- clusters and PDL
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// All threads of all CTAs of the cluster; release/acquire orders shared-memory
+// writes before the barrier with distributed-shared-memory reads after it.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel on the stream start its
+// prologue now / wait until the previous kernel's memory is visible.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
@@ -185,49 +244,71 @@ __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 // --------------------------------------------------------------- dequant
 // Code fields are placed so that codes of k and k+1 sit 16 bits apart (see the
 // tile layout in hq_layout.h).  OR-ing a field into the mantissa of a
-// floating-point constant yields (constant + code) exactly; one more packed
-// subtract removes the constant and the code offset.  The result is the exact
-// small integer q (int4: -8..7, ternary: -1..1) in both halves.
+// floating-point constant M yields the exact value M + code ("raw" values).
+// The exact dequantisers subtract M + offset with one packed op; the raw ones
+// skip it: the decode kernel feeds raw values straight into the MMA and
+// removes M + offset through a per-block activation row sum (an MMA with a
+// constant A operand that starts the accumulator).
+//
+// int4 word: pairs (e0,e1) (e2,e3) live in the low nibble of each byte
+// (nibbles 0/4 and 2/6), (e4,e5) (e6,e7) in the high nibble (1/5 and 3/7).
+// Outputs are in k order: o[0]=(e0,e1) o[1]=(e2,e3) o[2]=(e4,e5) o[3]=(e6,e7).
 
-// int4 -> 4 x half2 holding (q[k0],q[k1]) (q[k2],q[k3]) (q[k4],q[k5]) (q[k6],q[k7]).
-// With `unsigned_codes` the raw code u = q + 8 is produced instead.
+// fp16, raw.  o[0], o[1] = 1024 + u; o[2], o[3] = 1024 + 16 u (high-nibble
+// class, masked in place: the 1/16 goes onto the activation operand instead).
+__device__ __forceinline__ void raw_u4_f16(uint32_t w, uint32_t (&o)[4]) {
+    const uint32_t kMagic = 0x64006400u;  // 1024.0 in both halves
+    const uint32_t w8 = w >> 8;
+    o[0] = and_or(w, 0x000F000Fu, kMagic);
+    o[1] = and_or(w8, 0x000F000Fu, kMagic);
+    o[2] = and_or(w, 0x00F000F0u, kMagic);
+    o[3] = and_or(w8, 0x00F000F0u, kMagic);
+}
+
+// bf16, raw: 128 + u for all four pairs (bf16 has no room for the 16u form).
+__device__ __forceinline__ void raw_u4_bf16(uint32_t w, uint32_t (&o)[4]) {
+    const uint32_t kMagic = 0x43004300u;  // 128.0
+    o[0] = and_or(w, 0x000F000Fu, kMagic);
+    o[1] = and_or(w >> 8, 0x000F000Fu, kMagic);
+    o[2] = and_or(w >> 4, 0x000F000Fu, kMagic);
+    o[3] = and_or(w >> 12, 0x000F000Fu, kMagic);
+}
+
+// fp16, exact: q = u - 8 (or the code u itself when kUnsigned).
 template <bool kUnsigned = false>
 __device__ __forceinline__ void dequant_u4_f16(uint32_t w, uint32_t (&o)[4]) {
-    const uint32_t kMagic = 0x64006400u;          // 1024.0 in both halves
-    const uint32_t kSubLo = kUnsigned ? 0x64006400u : 0x64086408u;   // 1024 (+8)
-    const uint32_t kMulHi = 0x2C002C00u;          // 1/16
-    const uint32_t kAddHi = kUnsigned ? 0xD400D400u : 0xD480D480u;   // -64 (-72)
-    const uint32_t w8 = w >> 8;
-    uint32_t lo0 = and_or(w, 0x000F000Fu, kMagic);
-    uint32_t hi0 = and_or(w, 0x00F000F0u, kMagic);
-    uint32_t lo1 = and_or(w8, 0x000F000Fu, kMagic);
-    uint32_t hi1 = and_or(w8, 0x00F000F0u, kMagic);
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(lo0), "r"(kSubLo));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[1]) : "r"(hi0), "r"(kMulHi), "r"(kAddHi));
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(lo1), "r"(kSubLo));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[3]) : "r"(hi1), "r"(kMulHi), "r"(kAddHi));
+    const uint32_t kSubLo = kUnsigned ? 0x64006400u : 0x64086408u;  // 1024 (+8)
+    const uint32_t kMulHi = 0x2C002C00u;                             // 1/16
+    const uint32_t kAddHi = kUnsigned ? 0xD400D400u : 0xD480D480u;  // -64 (-72)
+    uint32_t r[4];
+    raw_u4_f16(w, r);
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(r[0]), "r"(kSubLo));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(r[1]), "r"(kSubLo));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[2]) : "r"(r[2]), "r"(kMulHi), "r"(kAddHi));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[3]) : "r"(r[3]), "r"(kMulHi), "r"(kAddHi));
 }
 
+// bf16, exact.
 template <bool kUnsigned = false>
 __device__ __forceinline__ void dequant_u4_bf16(uint32_t w, uint32_t (&o)[4]) {
-    const uint32_t kMagic = 0x43004300u;                             // 128.0
-    const uint32_t kSub = kUnsigned ? 0x43004300u : 0x43084308u;     // 128 (+8)
-    uint32_t a0 = and_or(w, 0x000F000Fu, kMagic);
-    uint32_t a1 = and_or(w >> 4, 0x000F000Fu, kMagic);
-    uint32_t a2 = and_or(w >> 8, 0x000F000Fu, kMagic);
-    uint32_t a3 = and_or(w >> 12, 0x000F000Fu, kMagic);
-    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(a0), "r"(kSub));
-    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[1]) : "r"(a1), "r"(kSub));
-    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(a2), "r"(kSub));
-    asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[3]) : "r"(a3), "r"(kSub));
+    const uint32_t kSub = kUnsigned ? 0x43004300u : 0x43084308u;  // 128 (+8)
+    uint32_t r[4];
+    raw_u4_bf16(w, r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) asm("sub.bf16x2 %0, %1, %2;" : "=r"(o[i]) : "r"(r[i]), "r"(kSub));
 }
 
-// ternary: pair p (codes of k=2p, 2p+1) sits at bits (2p, 16+2p).
+// ternary: pair p (codes of k=2p, 2p+1) sits at bits (2p, 16+2p); raw = M + c.
+template <bool kBF16>
+__device__ __forceinline__ uint32_t raw_t2_pair(uint32_t w, int p) {
+    return and_or(w >> (2 * p), 0x00030003u, kBF16 ? 0x43004300u : 0x64006400u);
+}
+
+// ternary, exact: t = c - 1.
 template <bool kBF16>
 __device__ __forceinline__ uint32_t dequant_t2_pair(uint32_t w, int p) {
-    const uint32_t kMagic = kBF16 ? 0x43004300u : 0x64006400u;
     const uint32_t kSub = kBF16 ? 0x43014301u : 0x64016401u;  // constant + 1
-    uint32_t a = and_or(w >> (2 * p), 0x00030003u, kMagic);
+    uint32_t a = raw_t2_pair<kBF16>(w, p);
     uint32_t o;
     if (kBF16)
         asm("sub.bf16x2 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(kSub));
@@ -236,18 +317,45 @@ __device__ __forceinline__ uint32_t dequant_t2_pair(uint32_t w, int p) {
     return o;
 }
 
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // ------------------------------------------------------------- mma.sync
+// D = A * B + C with separate C and D registers (no copy of a shared seed).
+template <bool kBF16>
+__device__ __forceinline__ void mma_16816_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                            const float (&c)[4]) {
+    if (kBF16) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+              "f"(c[3]));
+    } else {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+              "f"(c[3]));
+    }
+}
+
 // D(16x8,f32) += A(16x16) * B(16x8), fp16 or bf16 inputs.
 template <bool kBF16>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    // Plain (non-volatile) asm: a pure register operation the compiler may
+    // schedule freely, so independent MMA chains interleave.
     if (kBF16) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
     } else {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -3,25 +3,39 @@
 // Replaces kernel_marlin_gemm_int4_templated / _dynamic and the memset +
 // atomicAdd split-K of the reference (hydrogen/src/model/marlin_gemm.cu:130-322,
 // :556-601).  Design for B200:
-//   * Work = "units" (strip group of 128 columns, 64-k block).  The tile order
-//     makes any run of consecutive units one contiguous byte span, so each
-//     persistent CTA streams its unit range with large 1-D bulk copies (TMA
-//     engine) into a multi-stage shared-memory ring -- one elected producer
-//     thread, mbarrier full/empty handshakes, L2 evict-first hint.
+//   * Work = strip groups of 128 output columns.  A thread-block cluster of cs
+//     CTAs (cs in {1,2,4,8}, chosen so the grid fills the GPU) owns one strip
+//     group; CTA r of the cluster streams the group's k-blocks
+//     [r KB/cs, (r+1) KB/cs), which the tile order stores as one contiguous
+//     byte span.  One producer warp moves it with 1-D bulk copies (TMA engine)
+//     into a 4-stage shared-memory ring, two 64-k blocks per stage, together
+//     with each block's activation tile (one 2-D TMA box of 16 rows x 64 k,
+//     128-byte swizzled, rows >= M zero-filled) and group-scale row, so the
+//     consumer loop reads only shared memory.  L2 evict-first on the weights.
 //   * Four consumer warps each own two 16-column strips.  A lane's 16 bytes
-//     are exactly its A fragments for four m16n8k16 steps: register dequant
-//     (mask + OR into an fp16/bf16 exponent pattern, one packed subtract),
-//     tensor-core MMA with fp32 accumulation, and the group scale applied to
-//     each 64-k partial in fp32 (never rounded into the weight).
-//   * Split-K across CTAs is deterministic: each CTA writes its partial for a
-//     strip group to its own workspace slot; the last CTA to arrive (atomic
-//     counter) sums the slots in CTA order and writes C, then resets the
-//     counter to zero.  No memset, no float atomics, no spin-waits.
+//     are its A fragments for four m16n8k16 steps: codes are OR-ed into an
+//     fp16/bf16 exponent pattern (one LOP3 per pair) and fed to the tensor
+//     cores.  For M <= 8 the values go in raw (magic + code) and the magic
+//     offset times the activation row sum is pre-loaded into the accumulator
+//     by one MMA with a constant A operand; for M > 8 (where the legacy MMA
+//     rate binds) one packed subtract per pair gives exact q instead.  fp32
+//     accumulation; the group scale is applied in fp32 once per group within a
+//     stage (never rounded into the weight).
+//   * Split-K reduction through distributed shared memory: each CTA leaves its
+//     fp32 partial in its own shared memory, and after a cluster barrier CTA r
+//     sums 1/cs of the tile over the cs CTAs in rank order (deterministic) and
+//     writes C.  No workspace, no atomics, no memset.
+//   * Programmatic dependent launch: each CTA lets the next kernel on the
+//     stream start immediately; weights and scales (which no earlier kernel
+//     writes) are requested before griddepcontrol.wait, activations after it,
+//     so the next GEMM's weight stream overlaps this GEMM's tail.
 #include "hq_common.cuh"
 #include "hq_internal.h"
 #include "hq_layout.h"
+#include "hq_tmap.h"
 
 #include <algorithm>
+#include <cstring>
 #include <type_traits>
 
 namespace hq {
@@ -31,44 +45,54 @@ namespace {
 constexpr int kConsumerWarps = 4;
 constexpr int kStripsPerWarp = 2;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStageBytes = 8192;  // 2 int4 units / 4 ternary units of a full group
-constexpr int kStages = 6;
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 16;
+constexpr int kUPS = 2;  // 64-k blocks per stage
+constexpr int kMaxRows = 16;
 
-struct DecodeParams {
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// Shared-memory layout of one pipeline stage.
+template <int WBITS, typename AT, typename ST, bool kBias>
+struct Stage {
+    static constexpr int kCB = WBITS == 4 ? 512 : 256;
+    static constexpr int kWBytes = kUPS * kGroupStrips * kCB;  // weights of a full group
+    static constexpr bool kXTma = sizeof(AT) == 2;            // 16-bit activations: one TMA box per block
+    static constexpr int kXElt = (int)sizeof(AT);
+    static constexpr int kXRowBytes = kBlockK * kXElt;             // activation bytes per row and block
+    static constexpr int kXRow = kXTma ? 128 : kXRowBytes + 16;   // 128B-swizzled rows / padded rows
+    static constexpr int kXUnit = kMaxRows * kXRow;
+    static constexpr int kSElt = (int)sizeof(ST);
+    static constexpr int kSUnit = kGroupCols * kSElt;
+    static constexpr int kBUnit = kBias ? kGroupCols * 4 : 0;
+    static constexpr int kX = align_up(kWBytes, 1024);  // swizzled TMA destination: 1024-byte aligned
+    static constexpr int kS = kX + kUPS * kXUnit;
+    static constexpr int kB = kS + kUPS * kSUnit;
+    static constexpr int kBytes = align_up(kB + kUPS * kBUnit, 1024);
+    static constexpr int kStages = 4;
+    static constexpr int kSmem = kStages * kBytes + 1024 /* base alignment slack */ + 2 * kStages * 8;
+};
+
+struct alignas(64) DecodeParams {
+    CUtensorMap x_map;  // 16-bit activations [M][K]: box 64 x 16, 128B swizzle, OOB rows read zero
     const void* A;
     const uint8_t* W;
     const void* S;
     const float* bias;
     void* C;
-    float* partials;     // [(P + NSG)][M][128]
-    unsigned* counters;  // [NSG]
-    unsigned* err;       // device error word
+    unsigned* err;  // device error word
     int M, N, K, group;
-    long long U;
+    int cs;             // CTAs per strip group (cluster size)
+    int early_weights;  // stream weights/scales before the previous kernel finishes
 };
 
-// CTA that owns unit u when U units are split into P contiguous ranges
-// [floor(U p / P), floor(U (p+1) / P)).
-__device__ __forceinline__ int owner_of(long long u, long long U, int P) {
-    return (int)(((u + 1) * (long long)P - 1) / U);
-}
-
-template <typename AT>
-struct XFrag;
-
-// fp16 / bf16 activations: two 16-byte loads hold the 16 k this lane needs.
+// fp16 / bf16 activations: the 16 k (4 MMA steps) of one token row for this lane.
 template <typename AT>
 struct XFrag {
     uint4 a, b;
-    __device__ __forceinline__ void load(const AT* row, bool valid) {
-        if (valid) {
-            a = ldg128_nc(row);
-            b = ldg128_nc(row + 8);
-        } else {
-            a = make_uint4(0, 0, 0, 0);
-            b = a;
-        }
+    // TMA tile: row `r`, 16-byte chunks c at ((c ^ (r & 7)) << 4) (128B swizzle).
+    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t) {
+        const uint8_t* row = tile + r * 128;
+        a = *reinterpret_cast<const uint4*>(row + (((2 * t) ^ (r & 7)) << 4));
+        b = *reinterpret_cast<const uint4*>(row + (((2 * t + 1) ^ (r & 7)) << 4));
     }
     __device__ __forceinline__ uint32_t b0(int step) const {
         return step == 0 ? a.x : step == 1 ? a.z : step == 2 ? b.x : b.z;
@@ -78,14 +102,17 @@ struct XFrag {
     }
 };
 
-// fp32 activations: x = hi + lo with hi = fp16(x), lo = fp16(x - hi); two MMAs
-// per step keep the product accurate to ~2^-22 relative.
+// fp32 activations (padded rows): x = hi + lo with hi = fp16(x), lo = fp16(x - hi);
+// two MMAs per step keep the product accurate to ~2^-22 relative.
 struct XFragF32 {
     uint32_t hi[8], lo[8];
-    __device__ __forceinline__ void load(const float* row, bool valid) {
+    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t) {
+        const uint8_t* sp = tile + r * (kBlockK * 4 + 16) + 16 * t * 4;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            float4 v = valid ? *reinterpret_cast<const float4*>(row + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint4 q = *reinterpret_cast<const uint4*>(sp + 16 * i);
+            float4 v = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z),
+                                   __uint_as_float(q.w));
             __half2 h0 = __floats2half2_rn(v.x, v.y);
             __half2 h1 = __floats2half2_rn(v.z, v.w);
             float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
@@ -108,69 +135,107 @@ struct ComputeType<__nv_bfloat16> {
     static constexpr bool bf16 = true;
 };
 
-// A fragments (4 regs) of step `step` for this lane from its chunk words.
-template <int WBITS, bool kBF16, bool kUnsigned>
+// A fragments (4 regs) of each of the four m16n8k16 steps from a lane's chunk words.
+// kRaw: raw "magic + code" values (see hq_common.cuh); otherwise exact q (or u).
+template <int WBITS, bool kBF16, bool kUnsigned, bool kRaw>
 struct WFrag {
     uint32_t r[4][4];  // [step][reg]
+    __device__ __forceinline__ void expand(uint32_t w, uint32_t (&o)[4]) {
+        if constexpr (kRaw) {
+            if constexpr (kBF16)
+                raw_u4_bf16(w, o);
+            else
+                raw_u4_f16(w, o);
+        } else {
+            if constexpr (kBF16)
+                dequant_u4_bf16<kUnsigned>(w, o);
+            else
+                dequant_u4_f16<kUnsigned>(w, o);
+        }
+    }
     __device__ __forceinline__ void build(uint4 w) {
         if constexpr (WBITS == 4) {
             uint32_t g0[4], g8[4];
             // words: x = row g k0..7, y = row g k8..15, z = row g+8 k0..7, w = row g+8 k8..15
-            if constexpr (kBF16) {
-                dequant_u4_bf16<kUnsigned>(w.x, g0);
-                dequant_u4_bf16<kUnsigned>(w.z, g8);
-            } else {
-                dequant_u4_f16<kUnsigned>(w.x, g0);
-                dequant_u4_f16<kUnsigned>(w.z, g8);
-            }
+            expand(w.x, g0);
+            expand(w.z, g8);
             r[0][0] = g0[0]; r[0][1] = g8[0]; r[0][2] = g0[1]; r[0][3] = g8[1];
             r[1][0] = g0[2]; r[1][1] = g8[2]; r[1][2] = g0[3]; r[1][3] = g8[3];
-            if constexpr (kBF16) {
-                dequant_u4_bf16<kUnsigned>(w.y, g0);
-                dequant_u4_bf16<kUnsigned>(w.w, g8);
-            } else {
-                dequant_u4_f16<kUnsigned>(w.y, g0);
-                dequant_u4_f16<kUnsigned>(w.w, g8);
-            }
+            expand(w.y, g0);
+            expand(w.w, g8);
             r[2][0] = g0[0]; r[2][1] = g8[0]; r[2][2] = g0[1]; r[2][3] = g8[1];
             r[3][0] = g0[2]; r[3][1] = g8[2]; r[3][2] = g0[3]; r[3][3] = g8[3];
         } else {
             // words: x = row g k0..15, y = row g+8 k0..15
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
-                r[s][0] = dequant_t2_pair<kBF16>(w.x, 2 * s);
-                r[s][1] = dequant_t2_pair<kBF16>(w.y, 2 * s);
-                r[s][2] = dequant_t2_pair<kBF16>(w.x, 2 * s + 1);
-                r[s][3] = dequant_t2_pair<kBF16>(w.y, 2 * s + 1);
+                if constexpr (kRaw) {
+                    r[s][0] = raw_t2_pair<kBF16>(w.x, 2 * s);
+                    r[s][1] = raw_t2_pair<kBF16>(w.y, 2 * s);
+                    r[s][2] = raw_t2_pair<kBF16>(w.x, 2 * s + 1);
+                    r[s][3] = raw_t2_pair<kBF16>(w.y, 2 * s + 1);
+                } else {
+                    r[s][0] = dequant_t2_pair<kBF16>(w.x, 2 * s);
+                    r[s][1] = dequant_t2_pair<kBF16>(w.y, 2 * s);
+                    r[s][2] = dequant_t2_pair<kBF16>(w.x, 2 * s + 1);
+                    r[s][3] = dequant_t2_pair<kBF16>(w.y, 2 * s + 1);
+                }
             }
         }
     }
 };
 
+// Raw-value correction: the A constant whose MMA with step s's activation
+// fragment gives -(M + offset) * sum(x) (fp16 int4: odd steps see x/16 and
+// weights 1024 + 16u, hence 1152 = 72 * 16).
+template <int WBITS, bool kBF16>
+__device__ __forceinline__ uint32_t raw_corr_const(int step) {
+    if constexpr (WBITS == 4) {
+        if constexpr (kBF16) return 0xC308C308u;                   // -136
+        else return (step & 1) ? 0xE480E480u : 0xE408E408u;       // -1152 / -1032
+    } else {
+        return kBF16 ? 0xC301C301u : 0xE401E401u;                  // -129 / -1025
+    }
+}
+
 template <typename ST>
-__device__ __forceinline__ float load_scale(const void* S, size_t idx) {
-    return to_f32(__ldg(reinterpret_cast<const ST*>(S) + idx));
+__device__ __forceinline__ float lds_scale(const uint8_t* sp) {
+    return to_f32(*reinterpret_cast<const ST*>(sp));
 }
 
 template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
-__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const __grid_constant__ DecodeParams p) {
+    using L = Stage<WBITS, AT, ST, kBias>;
     constexpr bool kSplit = std::is_same<AT, float>::value;
     constexpr bool kBF16 = ComputeType<AT>::bf16;  // float activations compute in fp16
-    constexpr int kCB = WBITS == 4 ? 512 : 256;
+    constexpr int kCB = L::kCB;
     constexpr int kLaneBytes = kCB / 32;
+    constexpr int kStages = L::kStages;
+    // Raw path (M <= 8 with fp16/bf16 activations, symmetric weights): MMA on
+    // magic + code, offset removed by the per-block correction that seeds the
+    // accumulator.  M > 8 subtracts on the FMA pipe instead, sparing the
+    // legacy MMA rate which binds there.
+    constexpr bool kRaw = !kSplit && !kBias && MT == 1;
+    constexpr bool kHiScale = kRaw && WBITS == 4 && !kBF16;  // fp16 int4: x/16 on odd steps
 
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * L::kBytes);
     uint64_t* empty = full + kStages;
-    int* s_flag = reinterpret_cast<int*>(empty + kStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom geo(p.K, p.N, WBITS);
-    const int P = gridDim.x, pid = blockIdx.x;
-    const long long u0 = p.U * pid / P, u1 = p.U * (pid + 1) / P;
-    const int units_per_stage = kStageBytes / (kGroupStrips * kCB);
-    const int n_iters = (int)((u1 - u0 + units_per_stage - 1) / units_per_stage);
+    const int KB = geo.KB;
+    const int cs = p.cs;
+    const int sg = blockIdx.x / cs;
+    const int rank = cs > 1 ? (int)cluster_ctarank() : 0;
+    const int width = geo.width(sg);
+    const int kb_begin = rank * KB / cs, kb_end = (rank + 1) * KB / cs;
+    const int n_units = kb_end - kb_begin;
+    const int n_iters = (n_units + kUPS - 1) / kUPS;
+    const uint32_t unit_bytes = (uint32_t)width * kCB;  // one k-block of this strip group
+    const size_t off0 = geo.unit_offset((long long)sg * KB + kb_begin);
+    const int upg = p.group / kBlockK;  // k-blocks per scale group
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -179,36 +244,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         }
         fence_mbarrier_init();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        pdl_launch_dependents();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
-        // ------------------------------------------------------ producer
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            int issued = 0;
-            for (int it = 0; it < n_iters; ++it) {
-                const int slot = it % kStages;
-                const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-                if (!mbar_wait(&empty[slot], ph ^ 1u, p.err)) break;
-                const long long ua = u0 + (long long)it * units_per_stage;
-                const long long ub = ua + units_per_stage < u1 ? ua + units_per_stage : u1;
-                const size_t oa = geo.unit_offset(ua);
-                const uint32_t bytes = (uint32_t)(geo.unit_offset(ub) - oa);
-                mbar_arrive_expect_tx(&full[slot], bytes);
-                bulk_g2s_evict_first(ring + slot * kStageBytes, p.W + oa, bytes, &full[slot], pol);
-                issued = it + 1;
-            }
-            // Copies still in flight land before this thread leaves.
-            for (int it = issued - kStages < 0 ? 0 : issued - kStages; it < issued; ++it)
-                mbar_wait(&full[it % kStages], (uint32_t)(it / kStages) & 1u, p.err);
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------- consumers
-    const int g = lane >> 2, t = lane & 3;
-    const int KB = geo.KB;
     float acc[kStripsPerWarp][MT][4];
 #pragma unroll
     for (int j = 0; j < kStripsPerWarp; ++j)
@@ -217,222 +256,338 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[j][m][i] = 0.f;
 
-    long long cur_sg = u0 / KB;
-
-    auto flush = [&](long long sg) {
-        const int width = geo.width((int)sg);
-        const int f = owner_of(sg * KB, p.U, P);
-        const int l = owner_of((sg + 1) * KB - 1, p.U, P);
-        const int nc = l - f + 1;
-        OT* C = reinterpret_cast<OT*>(p.C);
-        if (nc == 1) {
+    if (warp == kConsumerWarps) {
+        // ---------------------------------------------------------- producer
+        const uint64_t pol = l2_policy_evict_first();
+        const uint8_t* Ab = reinterpret_cast<const uint8_t*>(p.A);
+        const uint8_t* Sb = reinterpret_cast<const uint8_t*>(p.S);
+        const uint8_t* Bb = reinterpret_cast<const uint8_t*>(p.bias);
+        const uint32_t cols = (uint32_t)width * kStripCols;
+        const uint32_t s_bytes = cols * L::kSElt, b_bytes = kBias ? cols * 4 : 0;
+        const uint32_t x_bytes = L::kXTma ? (uint32_t)L::kXUnit : (uint32_t)(p.M * L::kXRowBytes);
+        // Activation tiles of stage `it` (the part that depends on the previous kernel).
+        auto issue_x = [&](int it) {
+            const int slot = it % kStages;
+            uint8_t* st = ring + slot * L::kBytes;
+            const int nu = min(kUPS, n_units - it * kUPS);
+            if constexpr (L::kXTma) {
+                if (lane == 0)
+                    for (int ul = 0; ul < nu; ++ul)
+                        tma_load_2d(st + L::kX + ul * L::kXUnit, &p.x_map, (kb_begin + it * kUPS + ul) * kBlockK, 0,
+                                    &full[slot]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < kStripsPerWarp; ++j) {
-                const int sl = kStripsPerWarp * warp + j;
-                if (sl >= width) continue;
-                const int n = (int)(sg * kGroupCols) + sl * kStripCols + g;
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    const int tok = 8 * m + 2 * t;
-                    if (tok < p.M) {
-                        C[(size_t)tok * p.N + n] = from_f32<OT>(acc[j][m][0]);
-                        C[(size_t)tok * p.N + n + 8] = from_f32<OT>(acc[j][m][2]);
+                for (int ul = 0; ul < kUPS; ++ul) {
+                    if (ul < nu && lane < p.M) {
+                        const int kb = kb_begin + it * kUPS + ul;
+                        bulk_g2s(st + L::kX + ul * L::kXUnit + lane * L::kXRow,
+                                 Ab + ((size_t)lane * p.K + (size_t)kb * kBlockK) * L::kXElt, L::kXRowBytes,
+                                 &full[slot]);
                     }
-                    if (tok + 1 < p.M) {
-                        C[(size_t)(tok + 1) * p.N + n] = from_f32<OT>(acc[j][m][1]);
-                        C[(size_t)(tok + 1) * p.N + n + 8] = from_f32<OT>(acc[j][m][3]);
-                    }
                 }
             }
-            return;
-        }
-        float* part = p.partials + (size_t)(pid + sg) * p.M * kGroupCols;
-#pragma unroll
-        for (int j = 0; j < kStripsPerWarp; ++j) {
-            const int sl = kStripsPerWarp * warp + j;
-            if (sl >= width) continue;
-            const int nl = sl * kStripCols + g;
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const int tok = 8 * m + 2 * t;
-                if (tok < p.M) {
-                    part[tok * kGroupCols + nl] = acc[j][m][0];
-                    part[tok * kGroupCols + nl + 8] = acc[j][m][2];
-                }
-                if (tok + 1 < p.M) {
-                    part[(tok + 1) * kGroupCols + nl] = acc[j][m][1];
-                    part[(tok + 1) * kGroupCols + nl + 8] = acc[j][m][3];
-                }
+        };
+        const int early = p.early_weights ? min(kStages, n_iters) : 0;
+        if (!early) pdl_wait();
+        int issued = 0;
+        for (int it = 0; it < n_iters; ++it) {
+            const int slot = it % kStages;
+            const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait<256>(&empty[slot], ph ^ 1u, p.err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const int nu = min(kUPS, n_units - it * kUPS);
+            uint8_t* st = ring + slot * L::kBytes;
+            if (lane == 0) {
+                const uint32_t wbytes = (uint32_t)nu * unit_bytes;
+                mbar_arrive_expect_tx(&full[slot], wbytes + (uint32_t)nu * (x_bytes + s_bytes + b_bytes));
+                bulk_g2s_evict_first(st, p.W + off0 + (size_t)it * kUPS * unit_bytes, wbytes, &full[slot], pol);
             }
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(&p.counters[sg], 1u);
-            *s_flag = (old == (unsigned)(nc - 1));
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (*s_flag) {
-            __threadfence();
-            const int cols = width * kStripCols;
-            for (int e = threadIdx.x; e < p.M * kGroupCols; e += kConsumerWarps * 32) {
-                const int tok = e / kGroupCols, nl = e % kGroupCols;
-                if (nl >= cols) continue;
-                float s = 0.f;
-                for (int c = 0; c < nc; ++c)
-                    s += __ldcg(p.partials + (size_t)(f + c + sg) * p.M * kGroupCols + e);
-                C[(size_t)tok * p.N + sg * kGroupCols + nl] = from_f32<OT>(s);
+            __syncwarp();
+            // scale (and bias) row of each k-block: [group][the 128 columns]
+            if (lane >= 16 && lane < 16 + nu) {
+                const int i = lane - 16;
+                const int gi = (kb_begin + it * kUPS + i) / upg;
+                const size_t off = (size_t)gi * p.N + (size_t)sg * kGroupCols;
+                bulk_g2s(st + L::kS + i * L::kSUnit, Sb + off * L::kSElt, s_bytes, &full[slot]);
+                if constexpr (kBias) bulk_g2s(st + L::kB + i * L::kBUnit, Bb + off * 4, b_bytes, &full[slot]);
             }
-            if (threadIdx.x == 0) p.counters[sg] = 0u;
+            if (it >= early) {
+                issue_x(it);
+            } else if (it == early - 1) {
+                // First stages' weights are in flight; now wait for the previous
+                // kernel (which may have produced A) and add their activations.
+                pdl_wait();
+                for (int j = 0; j < early; ++j) issue_x(j);
+            }
+            issued = it + 1;
         }
-    };
+        if (issued < early) {  // timed out before the early stages were completed
+            pdl_wait();
+            for (int j = 0; j < issued; ++j) issue_x(j);
+        }
+        // Copies still in flight land before the ring is reused or the CTA exits.
+        if (lane == 0)
+            for (int it = issued - kStages < 0 ? 0 : issued - kStages; it < issued; ++it)
+                mbar_wait(&full[it % kStages], (uint32_t)(it / kStages) & 1u, p.err);
+        __syncwarp();
+    } else {
+        // -------------------------------------------------------- consumers
+        const int g = lane >> 2, t = lane & 3;
+        using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
+        const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
+        // After a timed-out wait the warp stops waiting but keeps the same
+        // control flow (results are garbage, the error word is set): every
+        // thread still reaches the barriers below, so nothing hangs.
+        bool waits_ok = true;
+        for (int it = 0; it < n_iters; ++it) {
+            const int slot = it % kStages;
+            if (waits_ok) waits_ok = mbar_wait<128>(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+            const int nu = min(kUPS, n_units - it * kUPS);
+            const int kb0 = kb_begin + it * kUPS;
+            // Both blocks of the stage in one scale group: one scale application.
+            const bool same = nu == 2 && (kb0 % upg) != upg - 1;
+            const uint8_t* stage = ring + slot * L::kBytes;
 
-    const AT* A = reinterpret_cast<const AT*>(p.A);
-    using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
-    const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
-
-    // After a timed-out wait the warp stops waiting but keeps the same control
-    // flow (results are garbage, the error word is set), so the named barriers
-    // of the split-K flush always see all consumer warps: no hang either way.
-    bool waits_ok = true;
-    for (int it = 0; it < n_iters; ++it) {
-        const int slot = it % kStages;
-        if (waits_ok) waits_ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
-        const long long ua = u0 + (long long)it * units_per_stage;
-        const long long ub = ua + units_per_stage < u1 ? ua + units_per_stage : u1;
-        const size_t oa = geo.unit_offset(ua);
-        const uint32_t stage_base = smem_u32(ring + slot * kStageBytes);
-        for (long long u = ua; u < ub; ++u) {
-            const long long sg = u / KB;
-            const int kb = (int)(u % KB);
-            if (sg != cur_sg) {
-                flush(cur_sg);
+            // Activation fragments (and raw-path corrections) of the stage's blocks.
+            XF xf[kUPS][MT];
+            float corr[kUPS][MT][4];
+            float xs[kUPS][MT][4];
 #pragma unroll
-                for (int j = 0; j < kStripsPerWarp; ++j)
+            for (int u = 0; u < kUPS; ++u) {
+                if (u >= nu) continue;
+                const uint8_t* tile = stage + L::kX + u * L::kXUnit;
 #pragma unroll
-                    for (int m = 0; m < MT; ++m)
+                for (int m = 0; m < MT; ++m) xf[u][m].load(tile, 8 * m + g, t);
+                // Rows >= M are zero (TMA fill) or stale (padded copies); either way
+                // they only feed MMA columns (tokens) that are never stored.
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) acc[j][m][i] = 0.f;
-                cur_sg = sg;
-            }
-            const int width = geo.width((int)sg);
-            const uint32_t unit_base = stage_base + (uint32_t)(geo.unit_offset(u) - oa);
-            XF xf[MT];
+                for (int m = 0; m < MT; ++m)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const int tok = 8 * m + g;
-                xf[m].load(A + (size_t)(tok < p.M ? tok : 0) * p.K + kb * kBlockK + 16 * t, tok < p.M);
-            }
-            const int gi = kb * kBlockK / p.group;
-            // Row sums of x over this 64-k block (only for the bias form).
-            float xs[MT][4];
-            if constexpr (kBias) {
-                const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+                    for (int i = 0; i < 4; ++i) corr[u][m][i] = 0.f;
+                if constexpr (kRaw) {
 #pragma unroll
-                for (int m = 0; m < MT; ++m) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) xs[m][i] = 0.f;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        if constexpr (kSplit) {
-                            mma_16816<false>(xs[m], ones, xf[m].hi[2 * s], xf[m].hi[2 * s + 1]);
-                            mma_16816<false>(xs[m], ones, xf[m].lo[2 * s], xf[m].lo[2 * s + 1]);
-                        } else {
-                            mma_16816<kBF16>(xs[m], ones, xf[m].b0(s), xf[m].b1(s));
+                    for (int m = 0; m < MT; ++m) {
+                        if constexpr (kHiScale) {
+                            const uint32_t kSixteenth = 0x2C002C00u;
+                            xf[u][m].a.z = hmul2_bits(xf[u][m].a.z, kSixteenth);
+                            xf[u][m].a.w = hmul2_bits(xf[u][m].a.w, kSixteenth);
+                            xf[u][m].b.z = hmul2_bits(xf[u][m].b.z, kSixteenth);
+                            xf[u][m].b.w = hmul2_bits(xf[u][m].b.w, kSixteenth);
                         }
-                    }
-                }
-            }
 #pragma unroll
-            for (int j = 0; j < kStripsPerWarp; ++j) {
-                const int sl = kStripsPerWarp * warp + j;
-                if (sl >= width) continue;
-                const uint32_t addr = unit_base + (uint32_t)(sl * kCB + lane * kLaneBytes);
-                uint4 wv;
-                if constexpr (WBITS == 4) {
-                    wv = lds128(addr);
-                } else {
-                    uint2 v = lds64(addr);
-                    wv = make_uint4(v.x, v.y, 0, 0);
-                }
-                const int n = (int)(sg * kGroupCols) + sl * kStripCols + g;
-                const size_t si = (size_t)gi * p.N + n;
-                float sc0, sc1;
-                if constexpr (std::is_same<ST, float>::value) {
-                    sc0 = __ldg(reinterpret_cast<const float*>(p.S) + si);
-                    sc1 = __ldg(reinterpret_cast<const float*>(p.S) + si + 8);
-                } else {
-                    sc0 = load_scale<ST>(p.S, si);
-                    sc1 = load_scale<ST>(p.S, si + 8);
-                }
-                WFrag<WBITS, kBF16, kBias> wf;
-                wf.build(wv);
-                float tmp[MT][4];
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) tmp[m][i] = 0.f;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        if constexpr (kSplit) {
-                            mma_16816<false>(tmp[m], wf.r[s], xf[m].hi[2 * s], xf[m].hi[2 * s + 1]);
-                            mma_16816<false>(tmp[m], wf.r[s], xf[m].lo[2 * s], xf[m].lo[2 * s + 1]);
-                        } else {
-                            mma_16816<kBF16>(tmp[m], wf.r[s], xf[m].b0(s), xf[m].b1(s));
+                        for (int s = 0; s < 4; ++s) {
+                            const uint32_t c = raw_corr_const<WBITS, kBF16>(s);
+                            const uint32_t ca[4] = {c, c, c, c};
+                            mma_16816<kBF16>(corr[u][m], ca, xf[u][m].b0(s), xf[u][m].b1(s));
                         }
                     }
                 }
                 if constexpr (kBias) {
-                    const float b0 = __ldg(p.bias + si), b1 = __ldg(p.bias + si + 8);
+                    const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        acc[j][m][0] += tmp[m][0] * sc0 + xs[m][0] * b0;
-                        acc[j][m][1] += tmp[m][1] * sc0 + xs[m][1] * b0;
-                        acc[j][m][2] += tmp[m][2] * sc1 + xs[m][2] * b1;
-                        acc[j][m][3] += tmp[m][3] * sc1 + xs[m][3] * b1;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) xs[u][m][i] = 0.f;
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            if constexpr (kSplit) {
+                                mma_16816<false>(xs[u][m], ones, xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                mma_16816<false>(xs[u][m], ones, xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
+                            } else {
+                                mma_16816<kBF16>(xs[u][m], ones, xf[u][m].b0(s), xf[u][m].b1(s));
+                            }
+                        }
+                    }
+                }
+            }
+
+#pragma unroll
+            for (int j = 0; j < kStripsPerWarp; ++j) {
+                const int sl = kStripsPerWarp * warp + j;
+                if (sl >= width) continue;
+                const int nl = sl * kStripCols + g;
+                float tacc[kUPS][MT][4];  // per-block partial sums (independent MMA chains)
+#pragma unroll
+                for (int u = 0; u < kUPS; ++u) {
+                    if (u >= nu) continue;
+                    const uint8_t* wp = stage + u * unit_bytes + sl * kCB + lane * kLaneBytes;
+                    uint4 wv;
+                    if constexpr (WBITS == 4) {
+                        wv = *reinterpret_cast<const uint4*>(wp);
+                    } else {
+                        const uint2 v = *reinterpret_cast<const uint2*>(wp);
+                        wv = make_uint4(v.x, v.y, 0, 0);
+                    }
+                    WFrag<WBITS, kBF16, kBias, kRaw> wf;
+                    wf.build(wv);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        if constexpr (kSplit) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) tacc[u][m][i] = 0.f;
+#pragma unroll
+                            for (int s = 0; s < 4; ++s) {
+                                mma_16816<false>(tacc[u][m], wf.r[s], xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                mma_16816<false>(tacc[u][m], wf.r[s], xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
+                            }
+                        } else {
+                            mma_16816_c<kBF16>(tacc[u][m], wf.r[0], xf[u][m].b0(0), xf[u][m].b1(0), corr[u][m]);
+#pragma unroll
+                            for (int s = 1; s < 4; ++s)
+                                mma_16816<kBF16>(tacc[u][m], wf.r[s], xf[u][m].b0(s), xf[u][m].b1(s));
+                        }
+                    }
+                }
+                // Apply the group scales (and the bias term of the reference form).
+                const uint8_t* s0p = stage + L::kS;
+                const float sa0 = lds_scale<ST>(s0p + nl * L::kSElt);
+                const float sa1 = lds_scale<ST>(s0p + (nl + 8) * L::kSElt);
+                if constexpr (kBias) {
+#pragma unroll
+                    for (int u = 0; u < kUPS; ++u) {
+                        if (u >= nu) continue;
+                        const float s0 = u ? lds_scale<ST>(s0p + L::kSUnit + nl * L::kSElt) : sa0;
+                        const float s1 = u ? lds_scale<ST>(s0p + L::kSUnit + (nl + 8) * L::kSElt) : sa1;
+                        const uint8_t* bp = stage + L::kB + u * L::kBUnit;
+                        const float b0 = lds_scale<float>(bp + nl * 4), b1 = lds_scale<float>(bp + (nl + 8) * 4);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            acc[j][m][0] += tacc[u][m][0] * s0 + xs[u][m][0] * b0;
+                            acc[j][m][1] += tacc[u][m][1] * s0 + xs[u][m][1] * b0;
+                            acc[j][m][2] += tacc[u][m][2] * s1 + xs[u][m][2] * b1;
+                            acc[j][m][3] += tacc[u][m][3] * s1 + xs[u][m][3] * b1;
+                        }
+                    }
+                } else if (same) {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        acc[j][m][0] = fmaf(tacc[0][m][0] + tacc[1][m][0], sa0, acc[j][m][0]);
+                        acc[j][m][1] = fmaf(tacc[0][m][1] + tacc[1][m][1], sa0, acc[j][m][1]);
+                        acc[j][m][2] = fmaf(tacc[0][m][2] + tacc[1][m][2], sa1, acc[j][m][2]);
+                        acc[j][m][3] = fmaf(tacc[0][m][3] + tacc[1][m][3], sa1, acc[j][m][3]);
                     }
                 } else {
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        acc[j][m][0] = fmaf(tmp[m][0], sc0, acc[j][m][0]);
-                        acc[j][m][1] = fmaf(tmp[m][1], sc0, acc[j][m][1]);
-                        acc[j][m][2] = fmaf(tmp[m][2], sc1, acc[j][m][2]);
-                        acc[j][m][3] = fmaf(tmp[m][3], sc1, acc[j][m][3]);
+                        acc[j][m][0] = fmaf(tacc[0][m][0], sa0, acc[j][m][0]);
+                        acc[j][m][1] = fmaf(tacc[0][m][1], sa0, acc[j][m][1]);
+                        acc[j][m][2] = fmaf(tacc[0][m][2], sa1, acc[j][m][2]);
+                        acc[j][m][3] = fmaf(tacc[0][m][3], sa1, acc[j][m][3]);
+                    }
+                    if (nu == 2) {
+                        const float sb0 = lds_scale<ST>(s0p + L::kSUnit + nl * L::kSElt);
+                        const float sb1 = lds_scale<ST>(s0p + L::kSUnit + (nl + 8) * L::kSElt);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            acc[j][m][0] = fmaf(tacc[1][m][0], sb0, acc[j][m][0]);
+                            acc[j][m][1] = fmaf(tacc[1][m][1], sb0, acc[j][m][1]);
+                            acc[j][m][2] = fmaf(tacc[1][m][2], sb1, acc[j][m][2]);
+                            acc[j][m][3] = fmaf(tacc[1][m][3], sb1, acc[j][m][3]);
+                        }
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (n_iters > 0) flush(cur_sg);
+
+    // ------------------------------------------------------------- epilogue
+    OT* C = reinterpret_cast<OT*>(p.C);
+    // Store a float4 of the fragment (strip sl, token tile m, lane) to C.
+    auto store_frag = [&](int sl, int m, int ln, float4 v) {
+        if (sl >= width) return;
+        const int n = sg * kGroupCols + sl * kStripCols + (ln >> 2);
+        const int tok = 8 * m + 2 * (ln & 3);
+        if (tok < p.M) {
+            C[(size_t)tok * p.N + n] = from_f32<OT>(v.x);
+            C[(size_t)tok * p.N + n + 8] = from_f32<OT>(v.z);
+        }
+        if (tok + 1 < p.M) {
+            C[(size_t)(tok + 1) * p.N + n] = from_f32<OT>(v.y);
+            C[(size_t)(tok + 1) * p.N + n + 8] = from_f32<OT>(v.w);
+        }
+    };
+    if (cs == 1) {
+        if (warp < kConsumerWarps) {
+#pragma unroll
+            for (int j = 0; j < kStripsPerWarp; ++j)
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    store_frag(kStripsPerWarp * warp + j, m, lane,
+                               make_float4(acc[j][m][0], acc[j][m][1], acc[j][m][2], acc[j][m][3]));
+        }
+        return;
+    }
+    // Cluster split-K: partial fragments to this CTA's shared memory (the ring,
+    // idle now: every issued copy has landed and been consumed), cluster
+    // barrier, then CTA `rank` reduces its 1/cs share over all cs CTAs in rank
+    // order and writes C; a second barrier keeps every CTA's shared memory
+    // alive until all remote reads are done.
+    constexpr int kFrags = kConsumerWarps * kStripsPerWarp * MT * 32;  // float4 per CTA
+    const uint32_t red = smem_u32(ring);
+    __syncthreads();
+    if (warp < kConsumerWarps) {
+#pragma unroll
+        for (int j = 0; j < kStripsPerWarp; ++j)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int i = ((warp * kStripsPerWarp + j) * MT + m) * 32 + lane;
+                sts_f4(red + 16 * i, make_float4(acc[j][m][0], acc[j][m][1], acc[j][m][2], acc[j][m][3]));
+            }
+    }
+    cluster_sync();
+    const int share = kFrags / cs;
+    for (int i = rank * share + (int)threadIdx.x; i < (rank + 1) * share; i += kThreads) {
+        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < cs; ++q) {
+            const float4 v = ld_dsmem_f4(mapa_shared(red + 16 * i, (uint32_t)q));
+            s4.x += v.x;
+            s4.y += v.y;
+            s4.z += v.z;
+            s4.w += v.w;
+        }
+        const int ln = i & 31, rest = i >> 5;
+        const int m = rest % MT, wj = rest / MT;
+        store_frag(wj, m, ln, s4);  // wj = warp * 2 + j = strip index
+    }
+    cluster_sync();
 }
 
 using KernelFn = void (*)(DecodeParams);
 
+struct KernelInfo {
+    KernelFn fn = nullptr;
+    int smem = 0;
+    bool x_tma = false;
+};
+
 template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
-KernelFn kernel_ptr() {
-    return decode_kernel<WBITS, MT, AT, ST, OT, kBias>;
+KernelInfo kernel_info() {
+    using L = Stage<WBITS, AT, ST, kBias>;
+    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias>, L::kSmem, L::kXTma};
 }
 
 // Output dtype: the activation's own 16-bit type or f32 (f32 activations: f32 out).
 template <int WBITS, int MT, typename AT, typename ST, bool kBias>
-KernelFn pick_out(DType c) {
-    if (c == DType::F32) return kernel_ptr<WBITS, MT, AT, ST, float, kBias>();
+KernelInfo pick_out(DType c) {
+    if (c == DType::F32) return kernel_info<WBITS, MT, AT, ST, float, kBias>();
     if constexpr (std::is_same<AT, __half>::value) {
-        if (c == DType::F16) return kernel_ptr<WBITS, MT, AT, ST, __half, kBias>();
+        if (c == DType::F16) return kernel_info<WBITS, MT, AT, ST, __half, kBias>();
     }
     if constexpr (std::is_same<AT, __nv_bfloat16>::value) {
-        if (c == DType::BF16) return kernel_ptr<WBITS, MT, AT, ST, __nv_bfloat16, kBias>();
+        if (c == DType::BF16) return kernel_info<WBITS, MT, AT, ST, __nv_bfloat16, kBias>();
     }
-    return nullptr;
+    return {};
 }
 
 // Supported (activation, scale, bias) combinations.  int4: (f16,f16), (bf16,bf16),
 // (f16|bf16, f32), (f32, f32) with or without bias for f16/f32 activations, and
 // (f32, f16).  Ternary: (f16,f16), (bf16,bf16).
 template <int WBITS, int MT>
-KernelFn pick(const GemmArgs& a) {
+KernelInfo pick(const GemmArgs& a) {
     const bool bias = a.bias != nullptr;
     if (a.a_dtype == DType::F16 && a.s_dtype == DType::F16 && !bias)
         return pick_out<WBITS, MT, __half, __half, false>(a.c_dtype);
@@ -450,53 +605,57 @@ KernelFn pick(const GemmArgs& a) {
         if (a.a_dtype == DType::F32 && a.s_dtype == DType::F16 && !bias)
             return pick_out<WBITS, MT, float, __half, false>(a.c_dtype);
     }
-    return nullptr;
+    return {};
 }
 
-KernelFn select_kernel(const GemmArgs& a) {
+KernelInfo select_kernel(const GemmArgs& a) {
     const int MT = a.M <= 8 ? 1 : 2;
     if (a.wbits == 4) return MT == 1 ? pick<4, 1>(a) : pick<4, 2>(a);
     return MT == 1 ? pick<2, 1>(a) : pick<2, 2>(a);
 }
 
-int grid_size(int M, long long U, int dev) {
-    const DeviceInfo& di = device_info(dev);
-    // Resident CTAs per SM is bounded by shared memory (48 KB ring each);
-    // decode_workspace_bytes relies on this bound (sm_count * 4).
-    const int per_sm = 4;
-    long long P = (long long)di.sm_count * per_sm;
-    // Larger M makes each split-K partial dearer; keep >= min_units per CTA.
-    const long long min_units = M <= 8 ? 4 : 8;
-    P = std::min(P, std::max<long long>(1, U / min_units));
-    P = std::min(P, U);
-    return (int)std::max<long long>(P, 1);
+constexpr int kMaxCtasPerSm = 4;
+
+// CTAs per strip group: the smallest power of two (<= 8, <= KB) whose grid
+// fills the resident CTA slots.
+int cluster_size(int N, int K, int wbits, int dev, int smem) {
+    const TileGeom geo(K, N, wbits);
+    int per_sm = (int)(233472 / (smem + 1024));
+    per_sm = std::max(1, std::min(per_sm, kMaxCtasPerSm));
+    const long long slots = (long long)device_info(dev).sm_count * per_sm;
+    int cs = 1;
+    while (cs < 8 && (long long)geo.NSG * cs * 10 < slots * 9 && cs * 2 <= geo.KB) cs *= 2;
+    return cs;
 }
+
+bool g_early_weights = true;
 
 }  // namespace
 
-bool decode_supported(const GemmArgs& a) { return select_kernel(a) != nullptr; }
+void set_decode_launch_overlap(bool on) { g_early_weights = on; }
 
-size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev) {
-    const TileGeom geo(K, N, wbits);
-    // Slot count bound for any launch with <= M rows: grid_size() never exceeds
-    // sm_count * 4, and a launch uses (grid + groups) slots of (rows x 128) floats.
-    const long long P = (long long)device_info(dev).sm_count * 4;
-    size_t part = (size_t)(P + geo.NSG) * (size_t)M * kGroupCols * sizeof(float);
-    size_t cnt = (size_t)geo.NSG * sizeof(unsigned);
-    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    return up(cnt) + up(part);
-}
+bool decode_supported(const GemmArgs& a) { return select_kernel(a).fn != nullptr; }
+
+size_t decode_workspace_bytes(int, int, int, int, int) { return 0; }
 
 cudaError_t launch_decode(const GemmArgs& a) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (a.M < 1 || a.M > kMaxRows) return cudaErrorInvalidValue;
     const TileGeom geo(a.K, a.N, a.wbits);
-    KernelFn fn = select_kernel(a);
-    if (!fn) return cudaErrorInvalidValue;
-    e = ensure_smem_attr(reinterpret_cast<const void*>(fn), dev, kSmemBytes);
+    const KernelInfo ki = select_kernel(a);
+    if (!ki.fn) return cudaErrorInvalidValue;
+    e = ensure_smem_attr(reinterpret_cast<const void*>(ki.fn), dev, ki.smem);
     if (e != cudaSuccess) return e;
     DecodeParams p;
+    memset(&p, 0, sizeof p);
+    if (ki.x_tma) {
+        // [M][K] 16-bit activations; a box is 64 k x 16 rows, rows >= M read zero.
+        e = make_tmap_2d(&p.x_map, a.A, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.M,
+                         (uint64_t)a.K * 2, kBlockK, kMaxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != cudaSuccess) return e;
+    }
     p.A = a.A;
     p.W = a.W;
     p.S = a.S;
@@ -506,14 +665,25 @@ cudaError_t launch_decode(const GemmArgs& a) {
     p.N = a.N;
     p.K = a.K;
     p.group = a.group;
-    p.U = geo.units();
     p.err = device_error_word(dev);
-    const int P = grid_size(a.M, p.U, dev);
-    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    p.counters = reinterpret_cast<unsigned*>(a.ws);
-    p.partials = reinterpret_cast<float*>(a.ws + up((size_t)geo.NSG * sizeof(unsigned)));
-    fn<<<P, kThreads, kSmemBytes, a.stream>>>(p);
-    return cudaGetLastError();
+    p.cs = cluster_size(a.N, a.K, a.wbits, dev, ki.smem);
+    p.early_weights = (g_early_weights && !a.weights_just_written) ? 1 : 0;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(geo.NSG * p.cs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)ki.smem;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, ki.fn, p);
 }
 
 }  // namespace hq

@@ -20,6 +20,7 @@ struct GemmArgs {
     void* C;
     DType c_dtype;
     int M, N, K, group;
+    bool weights_just_written;  // W was produced by the preceding kernel on the stream
     uint8_t* ws;  // 256-byte aligned workspace (after any re-tiled weights)
     size_t ws_bytes;
     cudaStream_t stream;
@@ -37,6 +38,9 @@ cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes);
 // Decode (M <= 16) HBM-streaming kernel.
 size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev);
 bool decode_supported(const GemmArgs& a);
+// Programmatic dependent launch lets a decode GEMM stream its weights while the
+// previous kernel on the stream finishes (on by default).
+void set_decode_launch_overlap(bool on);
 cudaError_t launch_decode(const GemmArgs& a);
 
 // Tensor-core (tcgen05) kernel for larger M.

@@ -11,7 +11,8 @@
 // Inside a chunk, lane l = 4g + t (g = 0..7, t = 0..3) of a warp owns
 // chunk_bytes/32 bytes at l*chunk_bytes/32, as little-endian 32-bit words:
 //   int4:    word j (0..3) = column 16s + g + 8*(j>>1), k = 64kb + 16t + 8*(j&1) + e,
-//            e = 0..7, 4-bit code u = q + 8 at nibble (e>>1) + 4*(e&1);
+//            e = 0..7, 4-bit code u = q + 8 at nibble u4_pos(e):
+//            e 0 1 2 3 4 5 6 7 -> nibble 0 4 2 6 1 5 3 7;
 //   ternary: word j (0..1) = column 16s + g + 8*j, k = 64kb + 16t + e, e = 0..15,
 //            2-bit code c = q + 1 at field (e>>1) + 8*(e&1).
 // A lane's words therefore hold exactly the A-fragment elements of
@@ -20,6 +21,10 @@
 // activation fragment, so the dot product is unchanged), and each word is 8
 // (int4) or 16 (ternary) consecutive k of one column, which is what the
 // tensor-core prefill kernel stores as one 16-byte K-major smem vector.
+// In an int4 word the codes of k-pairs (e0,e1) and (e2,e3) sit in the low
+// nibble of each byte (nibbles 0/4 and 2/6) and (e4,e5), (e6,e7) in the high
+// nibble (1/5 and 3/7): one MMA step draws all its pairs from one of the two
+// nibble classes, so a class is expanded with a single mask per pair.
 #pragma once
 
 #include <stddef.h>
@@ -73,7 +78,7 @@ struct TileGeom {
 };
 
 // Position (nibble or 2-bit field index) of in-word element e.
-HQ_HD int u4_pos(int e) { return (e >> 1) + 4 * (e & 1); }
+HQ_HD int u4_pos(int e) { return 2 * ((e >> 1) & 1) + ((e >> 2) & 1) + 4 * (e & 1); }
 HQ_HD int t2_pos(int e) { return (e >> 1) + 8 * (e & 1); }
 
 // Reorder the 8 nibbles of a linear word (k-offset e at nibble e) into tile order.

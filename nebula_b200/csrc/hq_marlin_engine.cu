@@ -48,7 +48,6 @@ void MarlinGemmEngine::ensure_workspace(uint32_t M) {
     // Room for the re-tiled weights of the drop-in path plus the kernel workspace.
     size_t need = hq_gemm_workspace_size((int)M, (int)config_.N, (int)config_.K, (int)config_.group_size,
                                          HQ_WFMT_MARLIN_QUAD);
-    if (need == 0) throw std::runtime_error("MarlinGemmEngine: unsupported shape");
     if (need <= workspace_bytes_) return;
     if (d_workspace_) cudaFree(d_workspace_);
     d_workspace_ = nullptr;

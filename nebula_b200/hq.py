@@ -75,11 +75,11 @@ def repack(src: torch.Tensor, src_fmt: int, dst_fmt: int, K: int, N: int, stream
 
 def make_workspace(M: int, N: int, K: int, group: int, wfmt: int, device) -> torch.Tensor:
     """Zero-filled workspace for hq_gemm (split-K partials + self-resetting counters)."""
+    if K <= 0 or N <= 0 or N % 16 or K % 64 or group <= 0 or K % group:
+        raise HQError(_lib.HQ_ERR_UNSUPPORTED_SHAPE, f"bad shape M={M} N={N} K={K} group={group}")
     with torch.cuda.device(device):
         nb = int(lib().hq_gemm_workspace_size(M, N, K, group, wfmt))
-    if nb == 0:
-        raise HQError(_lib.HQ_ERR_UNSUPPORTED_SHAPE, f"bad shape M={M} N={N} K={K} group={group}")
-    return torch.zeros(nb, dtype=torch.uint8, device=device)
+    return torch.zeros(max(nb, 16), dtype=torch.uint8, device=device)
 
 
 def gemm(A: torch.Tensor, W: torch.Tensor, scales: torch.Tensor, *, N: int, group: int = 128,

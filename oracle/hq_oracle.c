@@ -145,13 +145,16 @@ int hqo_unpack_linear_t2(const uint32_t* w, int8_t* t, int K, int N) {
  * offset l*CB/32, laid out as 32-bit little-endian words:
  *   int4 (4 words): word j holds row r = g + 8*(j>>1), k offsets
  *       16t + 8*(j&1) + e for e = 0..7, the 4-bit code u = q + 8 of offset e
- *       at nibble position (e>>1) + 4*(e&1);
+ *       at nibble position 2*((e>>1)&1) + ((e>>2)&1) + 4*(e&1)
+ *       (e = 0..7 -> nibbles 0 4 2 6 1 5 3 7);
  *   ternary (2 words): word j holds row r = g + 8*j, k offsets 16t + e for
  *       e = 0..15, the 2-bit code c = q + 1 of offset e at field position
  *       (e>>1) + 8*(e&1).
  * "row r" is output column 16s + r.  The field order puts the codes of k and
  * k+1 sixteen bits apart, which is what a single masked OR with a floating
- * point exponent pattern turns into a half2/bf162 pair.
+ * point exponent pattern turns into a half2/bf162 pair; in int4 words the
+ * pairs (0,1),(2,3) use the low nibble of each byte and (4,5),(6,7) the high
+ * nibble.
  */
 size_t hqo_tile_bytes(int K, int N, int wbits) {
     if (K <= 0 || N <= 0 || K % 64 || N % 16 || (wbits != 4 && wbits != 2)) return 0;
@@ -172,7 +175,7 @@ static size_t tile_locate(int k, int n, int K, int N, int wbits, int* shift) {
     if (wbits == 4) {
         const int half = (ko % 16) / 8, e = ko % 8;
         const int j = 2 * (r / 8) + half;
-        *shift = 4 * ((e >> 1) + 4 * (e & 1));
+        *shift = 4 * (2 * ((e >> 1) & 1) + ((e >> 2) & 1) + 4 * (e & 1));
         return lane_off + 4 * (size_t)j;
     } else {
         const int e = ko % 16;

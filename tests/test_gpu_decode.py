@@ -50,7 +50,9 @@ def test_decode_int4_parity(K, N, g, M, dtype):
     y16 = run_gemm(A, W, S, N, g, dtype)
     assert o.max_rel_err(y16, ref) <= TOL[dtype]
     y32 = run_gemm(A, W, S, N, g, dtype, out_dtype=torch.float32)
-    assert o.max_rel_err(y32, ref) <= 1e-5  # fp32 output: only accumulation-order differences
+    # fp32 output: accumulation order plus the raw-code offset correction (the MMA
+    # accumulates (magic + code) * x and subtracts magic * sum(x)), ~1e-5 relative.
+    assert o.max_rel_err(y32, ref) <= 1e-4
 
 
 @pytest.mark.parametrize("M", [1, 5, 16])
@@ -65,21 +67,45 @@ def test_reference_layouts_give_identical_results(M):
     assert np.array_equal(y_tile, y_lin) and np.array_equal(y_tile, y_quad)
 
 
-def test_decode_is_deterministic_and_leaves_counters_zero():
-    K, N, g, M = 17408, 5120, 128, 16
+@pytest.mark.parametrize("K,N", [(17408, 5120), (5120, 34816), (256, 48)])
+def test_decode_is_deterministic(K, N):
+    """Split-K over a thread-block cluster reduces in rank order: repeated calls are bitwise equal."""
+    g, M = 128, 16
     A, q, S = o.gen_int4_case(M, K, N, group=g, seed=5)
     W = cuda(o.pack_tile(q, 4), None)
     At, St = cuda(A, "f16"), cuda(S, "f16")
-    ws = hq.make_workspace(M, N, K, g, _lib.HQ_WFMT_TILE_U4, At.device)
-    y1 = hq.gemm(At, W, St, N=N, group=g, workspace=ws).clone()
-    y2 = hq.gemm(At, W, St, N=N, group=g, workspace=ws).clone()
+    assert _lib.lib().hq_gemm_workspace_size(M, N, K, g, _lib.HQ_WFMT_TILE_U4) == 0  # decode needs none
+    ys = [hq.gemm(At, W, St, N=N, group=g).clone() for _ in range(3)]
     torch.cuda.synchronize()
-    assert torch.equal(y1, y2)
-    nsg = (N // 16 + 7) // 8
-    assert int(ws[: nsg * 4].view(torch.int32).abs().sum()) == 0
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
     ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=g)
-    assert o.max_rel_err(y1.float().cpu().numpy(), ref) <= TOL["f16"]
+    assert o.max_rel_err(ys[0].float().cpu().numpy(), ref) <= TOL["f16"]
     hq.check_device_error()
+
+
+def test_launch_overlap_chain_matches_serial():
+    """A chain of dependent GEMMs (each output is the next input) gives the same result with the
+    launch overlap on and off: activations are read only after the previous kernel finished."""
+    K = N = 1024
+    rng = np.random.default_rng(3)
+    layers = []
+    for i in range(6):
+        _, q, S = o.gen_int4_case(1, K, N, group=128, seed=50 + i)
+        layers.append((cuda(o.pack_tile(q, 4), None), cuda(S * 0.25, "f16")))
+    x0 = cuda(o.round_to(rng.standard_normal((4, K)).astype(np.float32), "f16"), "f16")
+
+    def chain():
+        x = x0
+        for W, S in layers:
+            x = hq.gemm(x, W, S, N=N, group=128)
+        return x
+    outs = []
+    for flag in (1, 0, 1):
+        _lib.lib().hq_set_launch_overlap(flag)
+        outs.append(chain().clone())
+    torch.cuda.synchronize()
+    _lib.lib().hq_set_launch_overlap(1)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
 
 
 @pytest.mark.parametrize("name,K,N", [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816),
@@ -160,14 +186,23 @@ def test_tq1_0_gemv_golden_and_conversion():
     y = hq.tq1_0_gemv(x, blob, N)
     torch.cuda.synchronize()
     assert o.max_rel_err(y.cpu().numpy(), g["tq1_y"]) <= 1e-5
-    # offline conversion to the 2-bit tile order, then the decode kernel (fp16 activations)
-    tile, scales = hq.tq1_0_to_tile_t2(blob, K, N)
-    t_kn = np.ascontiguousarray(g["tq1_t"].T)
-    assert np.array_equal(tile.cpu().numpy(), o.pack_tile(t_kn, 2))
-    x16 = o.round_to(g["tq1_x"], "f16")
+
+
+@pytest.mark.parametrize("K,N", [(512, 48), (768, 144)])
+def test_tq1_0_to_tile_t2_then_gemm(K, N):
+    """Offline conversion of TQ1_0 into the 2-bit tile order (N % 16 == 0), then the decode kernel."""
+    rng = np.random.default_rng(N)
+    t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+    d[1, 0] = 0x7C00  # non-finite block scale: contributes nothing, as in the reference
+    blob = o.pack_tq1_0(t, d)
+    tile, scales = hq.tq1_0_to_tile_t2(cuda(blob, None), K, N)
+    torch.cuda.synchronize()
+    assert np.array_equal(tile.cpu().numpy(), o.pack_tile(np.ascontiguousarray(t.T), 2))
+    x16 = o.round_to(rng.standard_normal(K).astype(np.float32), "f16")
     y2 = hq.gemm(cuda(x16[None, :], "f16"), tile, scales, N=N, group=128, wfmt=_lib.HQ_WFMT_TILE_T2,
                  out_dtype=torch.float32)
-    ref2 = o.gemv_tq1_0(x16, g["tq1_blob"], K, N)
+    ref2 = o.gemv_tq1_0(x16, blob, K, N)
     assert o.max_rel_err(y2.cpu().numpy()[0], ref2) <= TOL["f16"]
 
 
