@@ -163,6 +163,121 @@ def run_reference_arm(args):
     return 0
 
 
+# ------------------------------------------- prefill / ternary sub-sweeps
+
+def _time_launches(torch, stream, fn, n_copies, reps=10, warmup=3):
+    """Average device time (ms) of fn(copy) over `reps` launches, CUDA events on `stream`."""
+    with torch.cuda.stream(stream):
+        for w in range(warmup):
+            fn(w % n_copies)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for r in range(reps):
+            fn(r % n_copies)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _gemm_call(L, _lib, A, a_dt, W, wfmt, S, s_dt, C, c_dt, M, N, K, ws, stream):
+    import ctypes
+    vp = ctypes.c_void_p
+    st = L.hq_gemm(vp(A.data_ptr()), a_dt, vp(W.data_ptr()), wfmt, vp(S.data_ptr()), s_dt, None, vp(C.data_ptr()),
+                   c_dt, M, N, K, GROUP, vp(ws.data_ptr()) if ws is not None else None,
+                   ws.numel() if ws is not None else 0, vp(stream.cuda_stream))
+    if st != 0:
+        raise RuntimeError(L.hq_last_error_string().decode())
+
+
+def prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args):
+    """the four 27B shapes at M in --prefill-ms, bf16 activations and scales,
+    int4 g128, bf16 out, through hq_gemm (the tcgen05 kernel for M > 16).  TFLOP/s = 2*M*N*K / time."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    Ms = [int(x) for x in args.prefill_ms.split(",") if x]
+    rows, tot_flop, tot_ms = [], 0.0, 0.0
+    for name, K, N in SHAPES:
+        Kl, Nl, copies = weights[name]
+        Sb = [S.bfloat16() for (_, S) in copies]
+        for M in Ms:
+            A = torch.randn((M, Kl), device=dev, generator=g).bfloat16()
+            C = torch.empty((M, Nl), device=dev, dtype=torch.bfloat16)
+            nb = int(L.hq_gemm_workspace_size(M, Nl, Kl, GROUP, _lib.HQ_WFMT_TILE_U4))
+            ws = torch.zeros(max(nb, 16), dtype=torch.uint8, device=dev)
+
+            def fn(c):
+                _gemm_call(L, _lib, A, _lib.HQ_BF16, copies[c][0], _lib.HQ_WFMT_TILE_U4, Sb[c], _lib.HQ_BF16, C,
+                           _lib.HQ_BF16, M, Nl, Kl, ws, stream)
+            reps = 10 if M <= 2048 else 4
+            ms = _time_launches(torch, stream, fn, len(copies), reps=reps)
+            flop = 2.0 * M * Nl * Kl
+            tot_flop += flop
+            tot_ms += ms
+            rows.append({"shape": name, "M": M, "K": Kl, "N": Nl, "us": round(ms * 1e3, 1),
+                         "TFLOPS": round(flop / (ms / 1e3) / 1e12, 1)})
+            del A, C, ws
+    tf = tot_flop / (tot_ms / 1e3) / 1e12
+    return {"metric": "prefill W4A16 GEMM TFLOP/s (BASELINE configs[2])", "value": tf, "unit": "TFLOP/s",
+            "dtype": "bf16", "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
+                                          "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
+                                          "peak_source": peaks["source"] + " (burst cuBLAS bf16)"},
+            "timing": "per GEMM: CUDA events around 10 launches (4 at M=8192) after 3 warm-up, 2 rotating weight "
+                      "copies; value = total FLOP / total time",
+            "per_gemm": rows}
+
+
+def _ternary_tile(torch, nbytes, dev, g):
+    f = torch.randint(0, 3, (nbytes, 4), dtype=torch.uint8, device=dev, generator=g)
+    return (f[:, 0] | (f[:, 1] << 2) | (f[:, 2] << 4) | (f[:, 3] << 6)).contiguous()
+
+
+def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
+    """ternary codes {-1,0,1} (2 bits), fp16 scales g128, fp16 activations, the 27B
+    shapes at M in {1, 16} (weight TB/s) and M = 2048 (TFLOP/s)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    rows = []
+    dec_bytes, dec_ms, pf_flop, pf_ms = 0.0, 0.0, 0.0, 0.0
+    for name, K, N in SHAPES:
+        copies = []
+        for c in range(args.copies):
+            W = _ternary_tile(torch, hq.weight_bytes(_lib.HQ_WFMT_TILE_T2, K, N), dev, g)
+            S = (torch.rand((K // GROUP, N), device=dev, generator=g) * 0.04 + 0.01).half()
+            copies.append((W, S))
+        for M in (1, 16, 2048):
+            A = torch.randn((M, K), device=dev, generator=g).half()
+            C = torch.empty((M, N), device=dev, dtype=torch.float16)
+            nb = int(L.hq_gemm_workspace_size(M, N, K, GROUP, _lib.HQ_WFMT_TILE_T2))
+            ws = torch.zeros(max(nb, 16), dtype=torch.uint8, device=dev)
+
+            def fn(c):
+                _gemm_call(L, _lib, A, _lib.HQ_F16, copies[c][0], _lib.HQ_WFMT_TILE_T2, copies[c][1], _lib.HQ_F16,
+                           C, _lib.HQ_F16, M, N, K, ws, stream)
+            ms = _time_launches(torch, stream, fn, len(copies), reps=20 if M <= 16 else 10)
+            wb = weight_bytes(K, N, wbits=2)
+            row = {"shape": name, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2)}
+            if M <= 16:
+                dec_bytes += wb
+                dec_ms += ms
+                row["GBps"] = round(wb / (ms / 1e3) / 1e9, 1)
+            else:
+                pf_flop += 2.0 * M * N * K
+                pf_ms += ms
+                row["TFLOPS"] = round(2.0 * M * N * K / (ms / 1e3) / 1e12, 1)
+            rows.append(row)
+            del A, C, ws
+    dec = dec_bytes / (dec_ms / 1e3) / 1e9
+    pf = pf_flop / (pf_ms / 1e3) / 1e12
+    return {"metric": "ternary W2A16 GEMM (BASELINE configs[3])",
+            "decode_GBps": dec, "decode_frac_hbm": dec / peaks["hbm_gbs"],
+            "prefill_TFLOPS": pf, "prefill_frac_tensor": pf / peaks["bf16_tflops"], "dtype": "f16",
+            "timing": "per GEMM: CUDA events around 20 (M<=16) / 10 launches after 3 warm-up, 2 rotating weight "
+                      "copies (not graph-captured, launch gaps included)",
+            "per_gemm": rows}
+
+
 # ---------------------------------------------------------------- GPU arm
 
 def main():
@@ -174,6 +289,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=2, help="rotating weight copies per shape (defeats L2)")
+    ap.add_argument("--no-extra", action="store_true", help="skip the prefill and ternary sweeps")
+    ap.add_argument("--prefill-ms", default="512,2048,8192", help="token counts of the prefill sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -369,6 +486,12 @@ def main():
 
     hq.check_device_error()
 
+    prefill = ternary = None
+    if world == 1 and not args.no_extra:
+        prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
+        ternary = ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
+        hq.check_device_error()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nth = os.cpu_count() or 1
@@ -405,6 +528,10 @@ def main():
             "clocks": clocks.summary(),
             "per_gemm": per,
         }
+        if prefill is not None:
+            line["prefill"] = prefill
+        if ternary is not None:
+            line["ternary"] = ternary
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
