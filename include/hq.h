@@ -130,6 +130,38 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype,
                          void* workspace, size_t ws_bytes,
                          hq_stream_t stream);
 
+/* Size of the scratch array that hq_gemm_noalloc uses in place of a workspace. */
+#define HQ_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/*
+ * hq_gemm for callers that cannot allocate device memory, e.g. a plugin
+ * inside a serving process that owns and budgets every byte of device memory
+ * (a pre-sized arena or another framework's allocator), where an extra
+ * cudaMalloc is not allowed or would stall the device mid-step.  Same
+ * arguments and results as hq_gemm minus the workspace: the workspace is a
+ * HQ_NOALLOC_SCRATCH_BYTES array compiled into this library.  This entry
+ * point allocates nothing and calls no allocating routine.
+ *   - Limit: a problem whose hq_gemm_workspace_size exceeds
+ *     HQ_NOALLOC_SCRATCH_BYTES fails with HQ_ERR_WORKSPACE_TOO_SMALL (reference
+ *     layouts need K*N/2 bytes for int4, K*N/4 for ternary; tile-order weights
+ *     need none).
+ *   - The first call on a device, with that device current, looks up the
+ *     array's device address and zero-fills it (synchronously); make that
+ *     first call before any stream capture.  The array then stays on that
+ *     device until the process exits.
+ *   - All calls on a device share the array, which keeps the previous call's
+ *     contents; calls whose GPU work overlaps (different streams, several host
+ *     threads) race on it, so keep them on one stream.
+ * No counterpart in the reference: it exists only for the callers above.
+ */
+HQ_API hq_status hq_gemm_noalloc(const void* A, hq_dtype a_dtype,
+                                 const void* Wq, hq_wfmt wfmt,
+                                 const void* scales, hq_dtype s_dtype,
+                                 const float* bias,
+                                 void* C, hq_dtype c_dtype,
+                                 int M, int N, int K, int group,
+                                 hq_stream_t stream);
+
 /*
  * Weight repack between formats, bit-exact in both directions.
  * Supported (src -> dst): LINEAR_U4 -> MARLIN_QUAD (the reference repack,

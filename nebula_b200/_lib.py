@@ -16,6 +16,7 @@ HQ_OK, HQ_ERR_INVALID_ARG, HQ_ERR_UNSUPPORTED_SHAPE, HQ_ERR_WORKSPACE_TOO_SMALL,
     HQ_ERR_TIMEOUT, HQ_ERR_MISALIGNED, HQ_ERR_UNSUPPORTED_DEVICE = range(8)
 HQ_F32, HQ_F16, HQ_BF16 = 0, 1, 2
 HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD, HQ_WFMT_TILE_U4, HQ_WFMT_LINEAR_T2, HQ_WFMT_TILE_T2, HQ_WFMT_TQ1_0 = range(6)
+HQ_NOALLOC_SCRATCH_BYTES = 64 << 20  # scratch array of hq_gemm_noalloc
 
 STATUS_NAMES = {0: "HQ_OK", 1: "HQ_ERR_INVALID_ARG", 2: "HQ_ERR_UNSUPPORTED_SHAPE", 3: "HQ_ERR_WORKSPACE_TOO_SMALL",
                 4: "HQ_ERR_CUDA", 5: "HQ_ERR_TIMEOUT", 6: "HQ_ERR_MISALIGNED", 7: "HQ_ERR_UNSUPPORTED_DEVICE"}
@@ -29,6 +30,7 @@ SIGNATURES = {
     "hq_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "hq_workspace_init": (_i, [_vp, _sz, _vp]),
     "hq_gemm": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "hq_gemm_noalloc": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "hq_repack_host": (_i, [_vp, _i, _vp, _i, _i, _i, _i]),
     "hq_repack_device": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "hq_tq1_0_gemv": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
