@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
             if (lane == 0) {
                 const uint32_t wbytes = (uint32_t)nu * unit_bytes;
                 mbar_arrive_expect_tx(&full[slot], wbytes + (uint32_t)nu * (x_bytes + s_bytes + b_bytes));
-                bulk_g2s_evict_first(st, p.W + off0 + (size_t)it * kUPS * unit_bytes, wbytes, &full[slot], pol);
+                bulk_g2s_hint(st, p.W + off0 + (size_t)it * kUPS * unit_bytes, wbytes, &full[slot], pol);
             }
             __syncwarp();
             // scale (and bias) row of each k-block: [group][the 128 columns]

@@ -1,28 +1,32 @@
-// hq_prefill.cu -- tensor-core (tcgen05 / TMEM) W4A16 / ternary GEMM for M > 16.
+// hq_prefill.cu -- tensor-core GEMM for M > 16 with the weights in tensor memory.
 //
 // The reference has no prefill GEMM (its decoder feeds the prompt one token at
-// a time, hydrogen/src/model/native_decoder.cu:1297); this kernel is the
-// B200 counterpart of the M >= 64 row of the quantized linear layer.
+// a time, hydrogen/src/model/native_decoder.cu:1297); this is the B200 kernel
+// for the M >= 64 rows of the quantized linear layer.
 //
-// One persistent CTA per SM walks output tiles of 128 tokens x 256 columns
-// (m-fastest, so the CTAs in flight share each n-tile's weights through L2):
-//   warp 4      producer: per 64-k block, a TMA box of the activations
-//               (128 x 64, 128-byte swizzle), the packed weights of the tile's
-//               two strip groups (1-D bulk copies of the tile order) and the
-//               group-scale row of the 256 columns, into a 4-stage ring;
-//   warps 6-13  dequantisers: each lane expands its 16 packed bytes (exact
-//               integer codes via the exponent-OR trick), multiplies by the
-//               column's group scale (16-bit packed mul) and stores 8-k
-//               vectors into the K-major 128B-swizzled B tile of a 3-stage
-//               ring, then fences the async proxy;
-//   warp 5      one thread issues tcgen05.mma (M=128, N=256, K=16, fp32
-//               accumulate in TMEM) and commits completions to the barriers;
-//               the warp also allocates / frees the 512 TMEM columns that hold
-//               two accumulators, so the epilogue of one tile overlaps the
-//               main loop of the next;
-//   warps 0-3   epilogue: tcgen05.ld of their 32 TMEM lanes (token rows),
-//               conversion and 64-byte row-segment stores of C.
-// Every barrier wait is bounded (see hq_common.cuh); nothing is allocated.
+// C^T tile = W_tile^T (128 output columns, tensor memory) x A_tile^T (256
+// tokens, shared memory): the MMA's M side is one strip group of the weights,
+// its N side the tokens.  The dequantised weights therefore go registers ->
+// tensor memory (tcgen05.st) and never through shared memory, whose bandwidth
+// the activation tiles (TMA in, MMA out) already use.
+//   warp 8      producer: per 64-k block, one TMA box of activations (64 k x
+//               256 tokens, 128-byte swizzle, rows >= M zero), the strip
+//               group's packed codes (one bulk copy of the tile order) and the
+//               group's scale row, into a 5-stage ring;
+//   warps 0-7   dequantisers, two sets of four alternating k-blocks; warp q of
+//               a set owns TMEM lanes [32q, 32q+32) = output columns: a thread
+//               gathers its column's 64 codes (four 8-byte loads), makes exact
+//               q, multiplies by the group scale (rounded to the activation
+//               type, as the tensor-core operand must be) and stores 32 packed
+//               pairs to an 8-deep ring of A buffers in tensor memory; after a
+//               tile's last k-block the same warps drain the accumulator
+//               (tcgen05.ld) and store C, set h taking tokens [128h, 128h+128);
+//   warp 9      one thread issues tcgen05.mma (M=128, N=256, K=16, A from
+//               tensor memory, fp32 accumulate in 256 TMEM columns) and
+//               commits completions; the warp owns the 512-column allocation.
+// Tiles (strip group x 256 tokens) are walked persistently, token tile
+// fastest, so the CTAs in flight share each strip group's codes through L2.
+// Every wait is bounded (hq_common.cuh); nothing is allocated.
 #include "hq_common.cuh"
 #include "hq_internal.h"
 #include "hq_layout.h"
@@ -36,34 +40,34 @@ namespace hq {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kEpiWarps = 4;  // warps 0..3 (TMEM lane quarters)
-constexpr int kProdWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kDqWarp0 = 6;
-constexpr int kDqWarps = 8;  // warps 6..13, two 16-column strips each
-constexpr int kThreads = (kDqWarp0 + kDqWarps) * 32;
-constexpr int kS1 = 4;  // activation + packed-weight + scale stages
-constexpr int kS2 = 3;  // dequantized weight stages
+constexpr int TM = 128;  // output columns per tile (MMA M)
+constexpr int TN = 256;  // tokens per tile (MMA N)
+constexpr int BK = 64;
+constexpr int kStages = 5;
+constexpr int kABufs = 8;
+constexpr int kDqWarps = 8;
+constexpr int kProdWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColD = 0;    // accumulator: 256 columns
+constexpr uint32_t kColA = 256;  // A ring: kColA + 32 * buf
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
 template <int WBITS>
-struct PLayout {
+struct TsLayout {
     static constexpr int kCB = WBITS == 4 ? 512 : 256;
-    static constexpr int kA = BM * BK * 2;                     // activation tile
-    static constexpr int kPacked = (BN / kStripCols) * kCB;    // 16 chunks
-    static constexpr int kScale = BN * 2;                      // 16-bit scales
-    static constexpr int kS1Bytes = align_up(kA + kPacked + kScale, 1024);
-    static constexpr int kB = BN * BK * 2;                     // dequantized weight tile
-    static constexpr int kOffB = kS1 * kS1Bytes;
-    static constexpr int kOffBar = kOffB + kS2 * kB;
-    static constexpr int kSmem = kOffBar + 256 + 1024;         // barriers + TMEM slot + alignment slack
+    static constexpr int kX = TN * BK * 2;                 // activation tile, 1024-aligned at stage start
+    static constexpr int kCodes = kGroupStrips * kCB;      // one strip group x 64 k
+    static constexpr int kScale = TM * 2;
+    static constexpr int kStage = align_up(kX + kCodes + kScale, 1024);
+    static constexpr int kRing = kStages * kStage;
+    static constexpr int kSmem = kRing + 256 + 1024;      // barriers + TMEM slot + alignment slack
 };
 
-struct alignas(64) PrefillParams {
-    CUtensorMap a_map;  // [M][K] 16-bit: box 64 x 128, 128B swizzle, rows >= M read zero
+struct alignas(64) PrefillTsParams {
+    CUtensorMap x_map;  // [M][K] 16-bit: box 64 x 256, 128B swizzle, rows >= M read zero
     const uint8_t* W;
     const void* S;
     void* C;
@@ -72,71 +76,32 @@ struct alignas(64) PrefillParams {
     int m_tiles, n_tiles;
 };
 
-template <typename T>
-__device__ __forceinline__ uint32_t scale_pair(const uint8_t* sp) {
-    const uint32_t v = *reinterpret_cast<const uint16_t*>(sp);
-    return v | (v << 16);
-}
-
 template <bool kBF16>
 __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t s) {
     return kBF16 ? bf16x2_mul(a, s) : hmul2_bits(a, s);
 }
 
 template <typename OT>
-__device__ __forceinline__ void store_row(OT* dst, const uint32_t (&v)[32], int ncols);
-
-template <>
-__device__ __forceinline__ void store_row<float>(float* dst, const uint32_t (&v)[32], int ncols) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        if (4 * i < ncols)
-            *reinterpret_cast<uint4*>(dst + 4 * i) = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-}
-
-template <typename T16>
-__device__ __forceinline__ void store_row16(T16* dst, const uint32_t (&v)[32], int ncols) {
-    uint32_t h[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        if constexpr (std::is_same<T16, __half>::value) {
-            __half2 x = __floats2half2_rn(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            h[i] = *reinterpret_cast<uint32_t*>(&x);
-        } else {
-            __nv_bfloat162 x = __floats2bfloat162_rn(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            h[i] = *reinterpret_cast<uint32_t*>(&x);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        if (8 * i < ncols)
-            *reinterpret_cast<uint4*>(dst + 8 * i) = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-}
-template <>
-__device__ __forceinline__ void store_row<__half>(__half* dst, const uint32_t (&v)[32], int ncols) {
-    store_row16(dst, v, ncols);
-}
-template <>
-__device__ __forceinline__ void store_row<__nv_bfloat16>(__nv_bfloat16* dst, const uint32_t (&v)[32], int ncols) {
-    store_row16(dst, v, ncols);
+__device__ __forceinline__ OT cvt_out(float v) {
+    return from_f32<OT>(v);
 }
 
 template <int WBITS, typename T, typename OT>
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
-    using L = PLayout<WBITS>;
+__global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_constant__ PrefillTsParams p) {
+    using L = TsLayout<WBITS>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr int kCB = L::kCB;
-    constexpr uint32_t kIdesc = umma_idesc_f16(kBF16, BM, BN);
+    constexpr uint32_t kIdesc = umma_idesc_f16(kBF16, TM, TN);
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint64_t* ld_full = reinterpret_cast<uint64_t*>(sm + L::kOffBar);
-    uint64_t* ld_empty = ld_full + kS1;
-    uint64_t* b_full = ld_empty + kS1;
-    uint64_t* b_empty = b_full + kS2;
-    uint64_t* acc_full = b_empty + kS2;
-    uint64_t* acc_empty = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint8_t* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + L::kRing);
+    uint64_t* empty = full + kStages;
+    uint64_t* a_full = empty + kStages;
+    uint64_t* a_empty = a_full + kABufs;
+    uint64_t* acc_full = a_empty + kABufs;
+    uint64_t* acc_empty = acc_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom geo(p.K, p.N, WBITS);
@@ -144,217 +109,192 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int num_tiles = p.m_tiles * p.n_tiles;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kS1; ++i) {
-            mbar_init(&ld_full[i], 1);
-            mbar_init(&ld_empty[i], 1 + kDqWarps);
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < kS2; ++i) {
-            mbar_init(&b_full[i], kDqWarps);
-            mbar_init(&b_empty[i], 1);
+        for (int i = 0; i < kABufs; ++i) {
+            mbar_init(&a_full[i], 4);  // the four warps of the set that expanded this k-block
+            mbar_init(&a_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kEpiWarps);
-        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kDqWarps);
         fence_mbarrier_init();
-        fence_async_smem();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
-        tc_fence_before();
     }
+    tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem = *tmem_slot;
 
     if (warp == kProdWarp) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_last();  // an n-tile's weights are re-read by every m-tile
+            const uint64_t pol = l2_policy_evict_last();  // codes are re-read by every token tile
             const uint8_t* Sb = reinterpret_cast<const uint8_t*>(p.S);
-            int kbc = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
-                const int m0 = mt * BM, n0 = nt * BN;
-                const int sg0 = n0 / kGroupCols;
-                const int w0 = geo.width(sg0);
-                const int w1 = sg0 + 1 < geo.NSG ? geo.width(sg0 + 1) : 0;
-                const int ncols = p.N - n0 < BN ? p.N - n0 : BN;
-                for (int kb = 0; kb < KB; ++kb, ++kbc) {
-                    const int s = kbc % kS1;
-                    if (!mbar_wait(&ld_empty[s], ((uint32_t)(kbc / kS1) & 1u) ^ 1u, p.err)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* st = sm + s * L::kS1Bytes;
-                    const uint32_t bytes = (uint32_t)(L::kA + (w0 + w1) * kCB + ncols * 2);
-                    mbar_arrive_expect_tx(&ld_full[s], bytes);
-                    tma_load_2d(st, &p.a_map, kb * BK, m0, &ld_full[s]);
-                    bulk_g2s_evict_first(st + L::kA, p.W + geo.unit_offset((long long)sg0 * KB + kb), w0 * kCB,
-                                         &ld_full[s], pol);
-                    if (w1)
-                        bulk_g2s_evict_first(st + L::kA + kGroupStrips * kCB,
-                                             p.W + geo.unit_offset((long long)(sg0 + 1) * KB + kb), w1 * kCB,
-                                             &ld_full[s], pol);
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int mt = tile % p.m_tiles, sg = tile / p.m_tiles;
+                const int width = geo.width(sg);
+                const uint32_t unit_bytes = (uint32_t)width * kCB;
+                const uint32_t s_bytes = (uint32_t)width * kStripCols * 2;
+                const size_t off = geo.unit_offset((long long)sg * KB);
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int slot = it % kStages;
+                    if (ok) ok = mbar_wait(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
+                    uint8_t* st = ring + slot * L::kStage;
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t)L::kX + unit_bytes + s_bytes);
+                    tma_load_2d(st, &p.x_map, kb * BK, mt * TN, &full[slot]);
+                    bulk_g2s_hint(st + L::kX, p.W + off + (size_t)kb * unit_bytes, unit_bytes, &full[slot], pol);
                     const int gi = kb * BK / p.group;
-                    bulk_g2s(st + L::kA + L::kPacked, Sb + ((size_t)gi * p.N + n0) * 2, ncols * 2, &ld_full[s]);
+                    bulk_g2s(st + L::kX + L::kCodes, Sb + ((size_t)gi * p.N + (size_t)sg * TM) * 2, s_bytes,
+                             &full[slot]);
                 }
             }
-            // Loads still in flight land before the CTA exits.
-            for (int k = kbc - kS1 < 0 ? 0 : kbc - kS1; k < kbc; ++k)
-                mbar_wait(&ld_full[k % kS1], (uint32_t)(k / kS1) & 1u, p.err);
+            // Copies still in flight land before the CTA exits.
+            for (int j = it - kStages < 0 ? 0 : it - kStages; j < it; ++j)
+                mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1u, p.err);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
-        // ----------------------------------------------------------- MMA issue
+        // ----------------------------------------------------------------- MMA
         if (lane == 0) {
-            int kbc = 0, tc = 0;
             bool ok = true;
+            int it = 0, tc = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
-                const int b = tc & 1;
-                if (ok) ok = mbar_wait(&acc_empty[b], ((uint32_t)(tc >> 1) & 1u) ^ 1u, p.err);
+                if (ok) ok = mbar_wait(acc_empty, ((uint32_t)tc & 1u) ^ 1u, p.err);
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-                for (int kb = 0; kb < KB; ++kb, ++kbc) {
-                    const int s1 = kbc % kS1, s2 = kbc % kS2;
-                    if (ok) ok = mbar_wait(&ld_full[s1], (uint32_t)(kbc / kS1) & 1u, p.err);
-                    if (ok) ok = mbar_wait(&b_full[s2], (uint32_t)(kbc / kS2) & 1u, p.err);
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int ab = it % kABufs, slot = it % kStages;
+                    // a_full implies full: the dequant warps saw the stage land first.
+                    if (ok) ok = mbar_wait<64>(&a_full[ab], (uint32_t)(it / kABufs) & 1u, p.err);
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sm + s1 * L::kS1Bytes);
-                    const uint32_t b_addr = smem_u32(sm + L::kOffB + s2 * L::kB);
+                    const uint32_t xs = smem_u32(ring + slot * L::kStage);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        umma_f16(d_tmem, sw128_kmajor_desc(a_addr + 32 * k), sw128_kmajor_desc(b_addr + 32 * k),
-                                 kIdesc, (kb | k) != 0);
-                    umma_commit(&ld_empty[s1]);
-                    umma_commit(&b_empty[s2]);
+                        umma_ts_f16(tmem + kColD, tmem + kColA + 32u * ab + 8u * k, sw128_kmajor_desc(xs + 32 * k),
+                                    kIdesc, (kb | k) != 0);
+                    umma_commit(&a_empty[ab]);
+                    umma_commit(&empty[slot]);
                 }
-                umma_commit(&acc_full[b]);
+                umma_commit(acc_full);
             }
         }
         __syncwarp();
-    } else if (warp >= kDqWarp0) {
-        // ------------------------------------------------------- dequantisers
-        const int dw = warp - kDqWarp0;
-        const int g = lane >> 2, t = lane & 3;
-        int kbc = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int nt = tile / p.m_tiles;
-            const int n0 = nt * BN;
-            const int sg0 = n0 / kGroupCols;
-            const int w0 = geo.width(sg0);
-            const int w1 = sg0 + 1 < geo.NSG ? geo.width(sg0 + 1) : 0;
-            for (int kb = 0; kb < KB; ++kb, ++kbc) {
-                const int s1 = kbc % kS1, s2 = kbc % kS2;
-                if (ok) ok = mbar_wait(&ld_full[s1], (uint32_t)(kbc / kS1) & 1u, p.err);
-                if (ok) ok = mbar_wait(&b_empty[s2], ((uint32_t)(kbc / kS2) & 1u) ^ 1u, p.err);
-                const uint8_t* packed = sm + s1 * L::kS1Bytes + L::kA;
-                const uint8_t* scales = packed + L::kPacked;
-                uint8_t* bt = sm + L::kOffB + s2 * L::kB;
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int c = 2 * dw + cc;  // strip within the tile, 0..15
-                    const int gs = c / kGroupStrips, sl = c % kGroupStrips;
-                    if (sl >= (gs ? w1 : w0)) continue;
-                    const uint8_t* src = packed + (gs * kGroupStrips + sl) * kCB + lane * (kCB / 32);
-                    const int r0 = c * kStripCols + g, r1 = r0 + 8;  // B-tile rows (output columns)
-                    const uint32_t sp0 = scale_pair<T>(scales + r0 * 2);
-                    const uint32_t sp1 = scale_pair<T>(scales + r1 * 2);
-                    uint32_t v0[8], v1[8];  // rows r0 / r1: k = 16t .. 16t+15 as 8 packed pairs
-                    if constexpr (WBITS == 4) {
-                        const uint4 w = *reinterpret_cast<const uint4*>(src);
-                        uint32_t o[4];
-                        if constexpr (kBF16) dequant_u4_bf16(w.x, o); else dequant_u4_f16(w.x, o);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v0[i] = mul2<kBF16>(o[i], sp0);
-                        if constexpr (kBF16) dequant_u4_bf16(w.y, o); else dequant_u4_f16(w.y, o);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v0[4 + i] = mul2<kBF16>(o[i], sp0);
-                        if constexpr (kBF16) dequant_u4_bf16(w.z, o); else dequant_u4_f16(w.z, o);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v1[i] = mul2<kBF16>(o[i], sp1);
-                        if constexpr (kBF16) dequant_u4_bf16(w.w, o); else dequant_u4_f16(w.w, o);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v1[4 + i] = mul2<kBF16>(o[i], sp1);
-                    } else {
-                        const uint2 w = *reinterpret_cast<const uint2*>(src);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            v0[i] = mul2<kBF16>(dequant_t2_pair<kBF16>(w.x, i), sp0);
-                            v1[i] = mul2<kBF16>(dequant_t2_pair<kBF16>(w.y, i), sp1);
-                        }
-                    }
-                    // 128B-swizzled K-major rows: 16-byte chunk q of row r at ((q ^ (r & 7)) << 4).
-                    uint8_t* row0 = bt + r0 * 128;
-                    uint8_t* row1 = bt + r1 * 128;
-                    *reinterpret_cast<uint4*>(row0 + (((2 * t) ^ (r0 & 7)) << 4)) = make_uint4(v0[0], v0[1], v0[2], v0[3]);
-                    *reinterpret_cast<uint4*>(row0 + (((2 * t + 1) ^ (r0 & 7)) << 4)) =
-                        make_uint4(v0[4], v0[5], v0[6], v0[7]);
-                    *reinterpret_cast<uint4*>(row1 + (((2 * t) ^ (r1 & 7)) << 4)) = make_uint4(v1[0], v1[1], v1[2], v1[3]);
-                    *reinterpret_cast<uint4*>(row1 + (((2 * t + 1) ^ (r1 & 7)) << 4)) =
-                        make_uint4(v1[4], v1[5], v1[6], v1[7]);
-                }
-                fence_async_smem();  // generic-proxy stores -> visible to the tensor core
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&b_full[s2]);
-                    mbar_arrive(&ld_empty[s1]);
-                }
-            }
-        }
     } else {
-        // ------------------------------------------------------------ epilogue
+        // ---------------------------------------------- dequant + epilogue
+        const int set = warp >> 2, q = warp & 3;
+        const int cl = 32 * q + lane;  // column within the strip group = TMEM lane
+        const int sl = cl >> 4;        // strip
+        const int c = lane & 15, g = c & 7, hh = c >> 3;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         OT* C = reinterpret_cast<OT*>(p.C);
-        int tc = 0;
         bool ok = true;
+        int it = 0, tc = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
-            const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
-            const int m0 = mt * BM, n0 = nt * BN;
-            const int b = tc & 1;
-            if (ok) ok = mbar_wait(&acc_full[b], (uint32_t)(tc >> 1) & 1u, p.err);
+            const int mt = tile % p.m_tiles, sg = tile / p.m_tiles;
+            const int width = geo.width(sg);
+            const bool valid = sl < width;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                if ((it & 1) != set) continue;
+                const int slot = it % kStages, ab = it % kABufs;
+                if (ok) ok = mbar_wait<128>(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+                if (ok) ok = mbar_wait<128>(&a_empty[ab], ((uint32_t)(it / kABufs) & 1u) ^ 1u, p.err);
+                __syncwarp();
+                tc_fence_after();
+                const uint8_t* st = ring + slot * L::kStage;
+                const uint8_t* codes = st + L::kX + sl * kCB;
+                uint32_t s2 = 0u;
+                if (valid) {
+                    const uint32_t v = *reinterpret_cast<const uint16_t*>(st + L::kX + L::kCodes + 2 * cl);
+                    s2 = v | (v << 16);
+                }
+                const uint32_t ta = tmem + lane_base + kColA + 32u * ab;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    uint32_t r[8];
+                    if constexpr (WBITS == 4) {
+                        uint2 w = make_uint2(0u, 0u);
+                        if (valid) w = *reinterpret_cast<const uint2*>(codes + (4 * g + t) * 16 + 8 * hh);
+                        uint32_t lo[4], hi[4];
+                        if constexpr (kBF16) {
+                            dequant_u4_bf16(w.x, lo);
+                            dequant_u4_bf16(w.y, hi);
+                        } else {
+                            dequant_u4_f16(w.x, lo);
+                            dequant_u4_f16(w.y, hi);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            r[e] = mul2<kBF16>(lo[e], s2);
+                            r[4 + e] = mul2<kBF16>(hi[e], s2);
+                        }
+                    } else {
+                        uint32_t w = 0u;
+                        if (valid) w = *reinterpret_cast<const uint32_t*>(codes + (4 * g + t) * 8 + 4 * hh);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) r[e] = mul2<kBF16>(dequant_t2_pair<kBF16>(w, e), s2);
+                    }
+                    tmem_st8(ta + 8u * t, r);  // k = 16t .. 16t+15 of this k-block
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[ab]);
+            }
+            // Epilogue of this tile: tokens [128 set, 128 set + 128) of column cl.
+            if (ok) ok = mbar_wait<256>(acc_full, (uint32_t)tc & 1u, p.err);
+            __syncwarp();
             tc_fence_after();
-            const int row = m0 + 32 * warp + lane;
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * warp) << 16) + (uint32_t)(b * BN);
+            const int col = sg * TM + cl;
+            const bool col_ok = valid;
 #pragma unroll 1
-            for (int cb = 0; cb < BN / 32; ++cb) {
+            for (int j = 0; j < 4; ++j) {
                 uint32_t v[32];
-                tmem_ld32(taddr + 32 * cb, v);
+                tmem_ld32(tmem + lane_base + kColD + 128u * set + 32u * j, v);
                 tmem_ld_wait();
-                const int col = n0 + 32 * cb;
-                const int ncols = p.N - col < 32 ? p.N - col : 32;
-                if (row < p.M && ncols > 0) store_row<OT>(C + (size_t)row * p.N + col, v, ncols);
+                const int tok0 = mt * TN + 128 * set + 32 * j;
+                if (col_ok) {
+#pragma unroll
+                    for (int r = 0; r < 32; ++r)
+                        if (tok0 + r < p.M) C[(size_t)(tok0 + r) * p.N + col] = cvt_out<OT>(__uint_as_float(v[r]));
+                }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[b]);
+            if (lane == 0) mbar_arrive(acc_empty);
         }
     }
 
+    tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
-using PrefillFn = void (*)(PrefillParams);
+using PrefillTsFn = void (*)(PrefillTsParams);
 
 template <int WBITS, typename T>
-PrefillFn pick_out(DType c) {
-    if (c == DType::F32) return prefill_kernel<WBITS, T, float>;
-    if (std::is_same<T, __half>::value && c == DType::F16) return prefill_kernel<WBITS, T, __half>;
-    if (std::is_same<T, __nv_bfloat16>::value && c == DType::BF16) return prefill_kernel<WBITS, T, __nv_bfloat16>;
+PrefillTsFn ts_pick_out(DType c) {
+    if (c == DType::F32) return prefill_ts_kernel<WBITS, T, float>;
+    if (std::is_same<T, __half>::value && c == DType::F16) return prefill_ts_kernel<WBITS, T, T>;
+    if (std::is_same<T, __nv_bfloat16>::value && c == DType::BF16) return prefill_ts_kernel<WBITS, T, T>;
     return nullptr;
 }
 
-PrefillFn select(const GemmArgs& a) {
+PrefillTsFn ts_select(const GemmArgs& a) {
     if (a.bias || a.s_dtype != a.a_dtype) return nullptr;
-    if (a.a_dtype == DType::F16) return a.wbits == 4 ? pick_out<4, __half>(a.c_dtype) : pick_out<2, __half>(a.c_dtype);
+    if (a.a_dtype == DType::F16)
+        return a.wbits == 4 ? ts_pick_out<4, __half>(a.c_dtype) : ts_pick_out<2, __half>(a.c_dtype);
     if (a.a_dtype == DType::BF16)
-        return a.wbits == 4 ? pick_out<4, __nv_bfloat16>(a.c_dtype) : pick_out<2, __nv_bfloat16>(a.c_dtype);
+        return a.wbits == 4 ? ts_pick_out<4, __nv_bfloat16>(a.c_dtype) : ts_pick_out<2, __nv_bfloat16>(a.c_dtype);
     return nullptr;
 }
 
@@ -362,21 +302,21 @@ PrefillFn select(const GemmArgs& a) {
 
 size_t prefill_workspace_bytes(int, int, int, int, int) { return 0; }
 
-bool prefill_supported(const GemmArgs& a) { return select(a) != nullptr; }
+bool prefill_supported(const GemmArgs& a) { return ts_select(a) != nullptr; }
 
 cudaError_t launch_prefill(const GemmArgs& a) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    PrefillFn fn = select(a);
+    PrefillTsFn fn = ts_select(a);
     if (!fn) return cudaErrorInvalidValue;
-    const int smem = a.wbits == 4 ? PLayout<4>::kSmem : PLayout<2>::kSmem;
+    const int smem = a.wbits == 4 ? TsLayout<4>::kSmem : TsLayout<2>::kSmem;
     e = ensure_smem_attr(reinterpret_cast<const void*>(fn), dev, smem);
     if (e != cudaSuccess) return e;
-    PrefillParams p;
+    PrefillTsParams p;
     memset(&p, 0, sizeof p);
-    e = make_tmap_2d(&p.a_map, a.A, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
-                     BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    e = make_tmap_2d(&p.x_map, a.A, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
+                     BK, TN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
     p.W = a.W;
     p.S = a.S;
@@ -386,8 +326,8 @@ cudaError_t launch_prefill(const GemmArgs& a) {
     p.N = a.N;
     p.K = a.K;
     p.group = a.group;
-    p.m_tiles = (a.M + BM - 1) / BM;
-    p.n_tiles = (a.N + BN - 1) / BN;
+    p.m_tiles = (a.M + TN - 1) / TN;
+    p.n_tiles = TileGeom(a.K, a.N, a.wbits).NSG;
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = std::min(tiles, device_info(dev).sm_count);
     fn<<<grid, kThreads, smem, a.stream>>>(p);
