@@ -11,8 +11,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <string>
 #include <utility>
 #include <vector>
@@ -52,6 +54,36 @@ cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e == cudaSuccess) done.insert(key);
     return e;
+}
+
+int max_active_clusters(const void* fn, int threads, int smem, int cs, int dev) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, int, int>, int> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(fn, threads, smem, cs, dev);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    if (cs > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return cache[key] = 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(cs * 64));
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int v = 0;
+    if (cudaOccupancyMaxActiveClusters(&v, fn, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        v = 0;
+    }
+    return cache[key] = v;
 }
 
 unsigned* device_error_word(int dev) {

@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
     // magic + code, offset removed by the per-block correction that seeds the
     // accumulator.  M > 8 subtracts on the FMA pipe instead, sparing the
     // legacy MMA rate which binds there.
-    constexpr bool kRaw = !kSplit && !kBias && MT == 1;
+    constexpr bool kRaw = false;
     constexpr bool kHiScale = kRaw && WBITS == 4 && !kBF16;  // fp16 int4: x/16 on odd steps
 
     extern __shared__ uint8_t smem_raw[];
@@ -539,8 +539,8 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
             }
     }
     cluster_sync();
-    const int share = kFrags / cs;
-    for (int i = rank * share + (int)threadIdx.x; i < (rank + 1) * share; i += kThreads) {
+    const int share = (kFrags + cs - 1) / cs;  // cs need not divide kFrags
+    for (int i = rank * share + (int)threadIdx.x; i < min(kFrags, (rank + 1) * share); i += kThreads) {
         float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int q = 0; q < cs; ++q) {
             const float4 v = ld_dsmem_f4(mapa_shared(red + 16 * i, (uint32_t)q));
@@ -614,18 +614,28 @@ KernelInfo select_kernel(const GemmArgs& a) {
     return MT == 1 ? pick<2, 1>(a) : pick<2, 2>(a);
 }
 
-constexpr int kMaxCtasPerSm = 4;
-
-// CTAs per strip group: the smallest power of two (<= 8, <= KB) whose grid
-// fills the resident CTA slots.
-int cluster_size(int N, int K, int wbits, int dev, int smem) {
+// CTAs per strip group, from {1, 2, 4, 8, 10, 12} (<= KB): the cs minimising
+// resident waves x k-blocks per CTA plus a reduction cost that grows with cs,
+// using the measured cluster occupancy of this kernel.  Narrow layers (N = 5120:
+// 40 strip groups) need clusters of more than 8 CTAs to put enough bytes in
+// flight per SM; larger clusters (14, 16) measured slower on B200.
+int cluster_size(const void* fn, int smem, int N, int K, int wbits, int dev) {
     const TileGeom geo(K, N, wbits);
-    int per_sm = (int)(233472 / (smem + 1024));
-    per_sm = std::max(1, std::min(per_sm, kMaxCtasPerSm));
-    const long long slots = (long long)device_info(dev).sm_count * per_sm;
-    int cs = 1;
-    while (cs < 8 && (long long)geo.NSG * cs * 10 < slots * 9 && cs * 2 <= geo.KB) cs *= 2;
-    return cs;
+    static const int kCandidates[] = {1, 2, 4, 8, 10, 12};
+    int best = 1;
+    long long best_cost = -1;
+    for (int cs : kCandidates) {
+        if (cs > geo.KB) break;
+        const int clusters = max_active_clusters(fn, kThreads, smem, cs, dev);
+        if (clusters <= 0) continue;
+        const long long waves = (geo.NSG + clusters - 1) / clusters;
+        const long long cost = waves * ((geo.KB + cs - 1) / cs) * 8 + 8 * cs;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = cs;
+        }
+    }
+    return best;
 }
 
 bool g_early_weights = true;
@@ -643,6 +653,11 @@ cudaError_t launch_decode(const GemmArgs& a) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (a.M < 1 || a.M > kMaxRows) return cudaErrorInvalidValue;
+    // M > 8 on wide layers runs on tcgen05: the mma.sync kernel needs two token
+    // tiles there and the tensor-memory kernel's cost does not depend on M.
+    // Narrow layers (few strip groups) and M <= 8 stream faster here.
+    if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= 48 && decode_tc_supported(a))
+        return launch_decode_tc(a, g_early_weights);
     const TileGeom geo(a.K, a.N, a.wbits);
     const KernelInfo ki = select_kernel(a);
     if (!ki.fn) return cudaErrorInvalidValue;
@@ -666,7 +681,7 @@ cudaError_t launch_decode(const GemmArgs& a) {
     p.K = a.K;
     p.group = a.group;
     p.err = device_error_word(dev);
-    p.cs = cluster_size(a.N, a.K, a.wbits, dev, ki.smem);
+    p.cs = cluster_size(reinterpret_cast<const void*>(ki.fn), ki.smem, a.N, a.K, a.wbits, dev);
     p.early_weights = (g_early_weights && !a.weights_just_written) ? 1 : 0;
 
     cudaLaunchConfig_t cfg = {};

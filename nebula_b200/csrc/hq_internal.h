@@ -34,6 +34,10 @@ struct DeviceInfo {
 const DeviceInfo& device_info(int dev);
 // Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
 cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes);
+// Clusters of `cs` CTAs of `fn` (threads, dynamic smem) that can be resident at
+// once on device `dev` (cached; cs > 8 enables non-portable cluster sizes on fn).
+// 0 when such a cluster cannot be launched.
+int max_active_clusters(const void* fn, int threads, int smem, int cs, int dev);
 
 // Decode (M <= 16) HBM-streaming kernel.
 size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev);
@@ -42,6 +46,10 @@ bool decode_supported(const GemmArgs& a);
 // previous kernel on the stream finishes (on by default).
 void set_decode_launch_overlap(bool on);
 cudaError_t launch_decode(const GemmArgs& a);
+// Decode on the tcgen05 tensor cores (16-bit activations and scales, no bias,
+// group a multiple of 128); launch_decode dispatches to it when supported.
+bool decode_tc_supported(const GemmArgs& a);
+cudaError_t launch_decode_tc(const GemmArgs& a, bool early_weights);
 
 // Tensor-core (tcgen05) kernel for larger M.
 size_t prefill_workspace_bytes(int M, int N, int K, int wbits, int dev);

@@ -36,7 +36,7 @@ def run_gemm(A, W_dev, S, N, group, dtype, wfmt=_lib.HQ_WFMT_TILE_U4, out_dtype=
     return Y.float().cpu().numpy()
 
 
-SHAPES = [(256, 48, 128), (512, 144, 64), (384, 256, 128), (1024, 1040, 128), (5120, 5120, 128)]
+SHAPES = [(256, 48, 128), (512, 144, 64), (384, 256, 128), (1024, 1040, 128), (5120, 5120, 128), (1024, 272, 256)]
 
 
 @pytest.mark.parametrize("K,N,g", SHAPES)
