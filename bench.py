@@ -12,6 +12,10 @@ With --gpus N > 1 (torchrun, one rank per GPU) the same sweep runs tensor-parall
 group boundaries with an NCCL all-reduce of the fp16 output after each; value is
 the whole layer's weight bytes per step / max-over-ranks step time.
 
+Sub-object "tp_stack" (every N): BASELINE configs[4], the 64-layer 27B linear stack
+tensor-parallel over the N ranks, 2304 rows (256 decode + a 2048-token prefill
+chunk) per step, NCCL all-reduce after O and down; TFLOP/s of the whole job.
+
 --impl reference times the reference's algorithm on the host cores: the CPU
 restatement in oracle/ (the reference has no CPU GEMM of its own), same metric.
 """
@@ -278,6 +282,102 @@ def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
             "per_gemm": rows}
 
 
+# ------------------------------------------------- TP layer stack
+
+def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
+    """the 64-layer 27B linear stack (QKV, O, gate_up, down per layer, int4 g128,
+    bf16 activations and scales, random weights from a per-(layer, projection, rank) seed), tensor-parallel
+    over the `world` ranks (nebula_b200.tp: column-parallel QKV / gate_up, row-parallel O / down with an
+    NCCL all-reduce of the bf16 output after each).  One step = one split-fuse batch of 256 decode rows +
+    a 2048-token prefill chunk = 2304 rows through every GEMM of every layer.  Inputs of O and down are
+    fixed synthetic tensors (attention and the MLP activation are outside this path)."""
+    from nebula_b200 import tp
+    rows, layers = 2304, args.stack_layers
+    g = torch.Generator(device=dev)
+    specs = {name: tp.shard_spec(name, K, N, world, rank) for name, K, N in tp.LAYER_SHAPES}
+    W = []
+    for layer in range(layers):
+        per = {}
+        for j, (name, K, N) in enumerate(tp.LAYER_SHAPES):
+            sp = specs[name]
+            g.manual_seed(1000003 * layer + 7919 * j + 104729 * rank + 17)
+            Wt = torch.randint(0, 256, (int(L.hq_weight_bytes(_lib.HQ_WFMT_TILE_U4, sp.K, sp.N)),), dtype=torch.uint8,
+                               device=dev, generator=g)
+            St = (torch.rand((sp.K // GROUP, sp.N), device=dev, generator=g) * 0.015 + 0.005).bfloat16()
+            per[name] = (Wt, St)
+        W.append(per)
+    g.manual_seed(4242 + rank)
+    X = {name: torch.randn((rows, specs[name].K), device=dev, generator=g).bfloat16() for name, _, _ in tp.LAYER_SHAPES}
+    Y = {name: torch.empty((rows, specs[name].N), device=dev, dtype=torch.bfloat16) for name, _, _ in tp.LAYER_SHAPES}
+    ws_bytes = max(int(L.hq_gemm_workspace_size(rows, specs[n].N, specs[n].K, GROUP, _lib.HQ_WFMT_TILE_U4))
+                   for n, _, _ in tp.LAYER_SHAPES)
+    ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+
+    def step():
+        for layer in range(layers):
+            for name, _, _ in tp.LAYER_SHAPES:
+                sp = specs[name]
+                Wt, St = W[layer][name]
+                _gemm_call(L, _lib, X[name], _lib.HQ_BF16, Wt, _lib.HQ_WFMT_TILE_U4, St, _lib.HQ_BF16, Y[name],
+                           _lib.HQ_BF16, rows, sp.N, sp.K, ws, stream)
+                if sp.row_parallel and world > 1:
+                    dist.all_reduce(Y[name])
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = args.stack_steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    flop = 2.0 * rows * sum(K * N for _, K, N in tp.LAYER_SHAPES) * layers
+    tf = flop / (ms / 1e3) / 1e12
+    del W, X, Y, ws
+    torch.cuda.empty_cache()
+    return {"metric": "TP layer-stack TFLOP/s (BASELINE configs[4])", "value": tf, "unit": "TFLOP/s",
+            "tokens_per_s": rows / (ms / 1e3), "ms_per_step": ms, "n_gpus": world, "layers": layers,
+            "rows_per_step": rows, "scaling": "strong", "dtype": "bf16",
+            "frac_of_n_x_peak": tf / (world * peaks["bf16_tflops"]),
+            "timing": f"{steps} steps after 2 warm-up, CUDA events on the compute stream, max over ranks; "
+                      "64 x 4 hq_gemm launches + 128 NCCL all-reduces per step at TP"}
+
+
+def run_case(args):
+    """One hq_gemm problem launched --steps times (for ncu captures of a single kernel)."""
+    import torch
+    from nebula_b200 import _lib, hq
+    f = args.case.split(",")
+    K, N, M = int(f[0]), int(f[1]), int(f[2])
+    dt = f[3] if len(f) > 3 else "f16"
+    wfmt = _lib.HQ_WFMT_TILE_T2 if len(f) > 4 and f[4] == "t2" else _lib.HQ_WFMT_TILE_U4
+    tdt = torch.float16 if dt == "f16" else torch.bfloat16
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    W = torch.randint(0, 256, (hq.weight_bytes(wfmt, K, N),), dtype=torch.uint8, device=dev, generator=g)
+    S = (torch.rand((K // GROUP, N), device=dev, generator=g) * 0.015 + 0.005).to(tdt)
+    A = torch.randn((M, K), device=dev, generator=g).to(tdt)
+    for _ in range(args.steps):
+        y = hq.gemm(A, W, S, N=N, group=GROUP, wfmt=wfmt)
+    torch.cuda.synchronize()
+    hq.check_device_error()
+    print(json.dumps({"case": args.case, "checksum": float(y.float().abs().sum())}))
+    return 0
+
+
 # ---------------------------------------------------------------- GPU arm
 
 def main():
@@ -290,12 +390,19 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=2, help="rotating weight copies per shape (defeats L2)")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill and ternary sweeps")
+    ap.add_argument("--no-stack", action="store_true", help="skip the TP layer stack (configs[4])")
+    ap.add_argument("--case", default=None,
+                    help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits")
+    ap.add_argument("--stack-layers", type=int, default=64)
+    ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--prefill-ms", default="512,2048,8192", help="token counts of the prefill sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.case:
+        return run_case(args)
 
     import torch
     import torch.distributed as dist
@@ -486,6 +593,11 @@ def main():
 
     hq.check_device_error()
 
+    stack = None
+    if not args.no_stack:
+        stack = tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args)
+        hq.check_device_error()
+
     prefill = ternary = None
     if world == 1 and not args.no_extra:
         prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
@@ -528,6 +640,8 @@ def main():
             "clocks": clocks.summary(),
             "per_gemm": per,
         }
+        if stack is not None:
+            line["tp_stack"] = stack
         if prefill is not None:
             line["prefill"] = prefill
         if ternary is not None:
