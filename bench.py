@@ -542,11 +542,15 @@ def main():
     kern_s = sum(acc_ms) / reps / 1e3
     achieved = kern_bytes / kern_s / 1e9
 
+    # DRAM bytes per launch: the ratio measured by ncu on the dominant launch
+    # (dram__bytes_read + dram__bytes_write over the algorithmic bytes, recorded
+    # in profiles/decode_traffic.json) times the average algorithmic bytes per launch.
     traffic = None
     tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get("traffic_ratio")
+            ratio = json.load(open(tp)).get("traffic_ratio")
+            traffic = ratio * kern_bytes / len(gemms) if ratio else None
         except (ValueError, OSError):
             traffic = None
 
@@ -632,7 +636,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": peaks["source"], "frac_of_nominal_8000": achieved / 8000.0,
-                         "kernel": "hq decode_kernel (bulk-copy ring + mma.sync dequant)",
+                         "kernel": "hq decode kernels (mma.sync for M <= 8 / narrow layers, tcgen05 for M > 8 on wide layers)", "traffic_unit": "bytes per launch (avg)",
                          "algorithmic_bytes_per_step": kern_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
