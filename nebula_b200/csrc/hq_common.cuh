@@ -324,6 +324,63 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
     return d;
 }
 
+// ----------------------------------------------- column gather (tile order)
+// The codes of one output column c = g + 8 hh of a 64-k chunk (tile order, see
+// hq_layout.h) live in the fragments of lanes 4g .. 4g+3, 16 k each.  A thread
+// that owns column c (tensor-memory operand layout: one column per lane) reads
+// the four fragments starting at a rotated lane, `rot`, chosen so that the 16
+// threads of a half-warp (int4, 8-byte loads) or the 32 threads of a warp
+// (ternary, 4-byte loads) touch distinct banks; the rotation is then undone in
+// registers.  Output: the column's words in k order, w[i] = k 8i .. 8i+7 (int4)
+// or k 16i .. 16i+15 (ternary).
+template <typename T>
+__device__ __forceinline__ void unrotate4(T (&v)[4], int rot) {
+    // v[j] holds fragment (j + rot) & 3; afterwards v[t] holds fragment t.
+    if (rot & 1) {
+        const T a = v[3];
+        v[3] = v[2];
+        v[2] = v[1];
+        v[1] = v[0];
+        v[0] = a;
+    }
+    if (rot & 2) {
+        T a = v[0];
+        v[0] = v[2];
+        v[2] = a;
+        a = v[1];
+        v[1] = v[3];
+        v[3] = a;
+    }
+}
+
+// int4: rot = g >> 1 (lane = 16 s' + 8 hh + g within the warp).
+__device__ __forceinline__ void gather_column_u4(const uint8_t* chunk, int g, int hh, int rot, bool valid,
+                                                 uint32_t (&w)[8]) {
+    uint2 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        v[j] = valid ? *reinterpret_cast<const uint2*>(chunk + (4 * g + ((j + rot) & 3)) * 16 + 8 * hh)
+                     : make_uint2(0u, 0u);
+    unrotate4(v, rot);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        w[2 * t] = v[t].x;
+        w[2 * t + 1] = v[t].y;
+    }
+}
+
+// ternary: rot = (g >> 2) + 2 s' (lane = 16 s' + 8 hh + g within the warp).
+__device__ __forceinline__ void gather_column_t2(const uint8_t* chunk, int g, int hh, int rot, bool valid,
+                                                 uint32_t (&w)[4]) {
+    uint32_t v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        v[j] = valid ? *reinterpret_cast<const uint32_t*>(chunk + (4 * g + ((j + rot) & 3)) * 8 + 4 * hh) : 0u;
+    unrotate4(v, rot);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) w[t] = v[t];
+}
+
 // ------------------------------------------------------------- tcgen05
 // Tensor-memory allocation (one warp, .sync.aligned), MMA issue (one thread),
 // completion commits to mbarriers, and TMEM -> register loads.

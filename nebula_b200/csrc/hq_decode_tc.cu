@@ -16,7 +16,8 @@
 //   * Eight dequant warps, two sets of four; set h expands k-block h of every
 //     stage.  Warp q of a set owns TMEM lanes [32q, 32q+32) = output columns,
 //     one column per thread: the thread gathers its column's 64 codes (four
-//     8-byte loads from the lane fragments that hold them), makes exact q
+//     8-byte loads from the lane fragments that hold them, start lane rotated
+//     so a half-warp hits distinct banks), makes exact q
 //     (exponent-OR plus one packed subtract per pair) and stores 32 packed
 //     pairs to its set's A buffer with tcgen05.st.
 //   * Two issuing threads (warps 9 and 10, one per set) issue, for their
@@ -255,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
         const int set = warp >> 2, q = warp & 3;
         const int sl = 2 * q + (lane >> 4);  // strip of the group
         const int c = lane & 15, g = c & 7, hh = c >> 3;
+        const int rot = WBITS == 4 ? (g >> 1) : ((g >> 2) + 2 * (lane >> 4));  // bank-conflict-free gather
         const bool valid = sl < width;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         float sc_prev = 0.f;
@@ -288,12 +290,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
             const float sc =
                 valid ? scale_f32<kBF16>(*reinterpret_cast<const uint16_t*>(st + L::kS + 2 * (16 * sl + c))) : 0.f;
             const uint32_t ta = tmem + lane_base + col_a(set, b);
+            uint32_t cw[WBITS == 4 ? 8 : 4];  // this column's codes, k order
+            if constexpr (WBITS == 4) gather_column_u4(wu, g, hh, rot, valid, cw);
+            else gather_column_t2(wu, g, hh, rot, valid, cw);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {  // tcgen05.st takes one warp-uniform column: k = 16t .. 16t+15
                 uint32_t r[8];
                 if constexpr (WBITS == 4) {
-                    uint2 w = make_uint2(0u, 0u);
-                    if (valid) w = *reinterpret_cast<const uint2*>(wu + (4 * g + t) * 16 + 8 * hh);
+                    const uint2 w = make_uint2(cw[2 * t], cw[2 * t + 1]);
                     uint32_t lo[4], hi[4];
                     if constexpr (kBF16) {
                         dequant_u4_bf16(w.x, lo);
@@ -308,8 +312,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
                         r[4 + e] = hi[e];
                     }
                 } else {
-                    uint32_t w = 0u;
-                    if (valid) w = *reinterpret_cast<const uint32_t*>(wu + (4 * g + t) * 8 + 4 * hh);
+                    const uint32_t w = cw[t];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) r[e] = dequant_t2_pair<kBF16>(w, e);
                 }

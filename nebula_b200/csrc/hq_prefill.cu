@@ -12,10 +12,11 @@
 //   warp 8      producer: per 64-k block, one TMA box of activations (64 k x
 //               256 tokens, 128-byte swizzle, rows >= M zero), the strip
 //               group's packed codes (one bulk copy of the tile order) and the
-//               group's scale row, into a 5-stage ring;
+//               group's scale row, into a 6-stage ring;
 //   warps 0-7   dequantisers, two sets of four alternating k-blocks; warp q of
 //               a set owns TMEM lanes [32q, 32q+32) = output columns: a thread
-//               gathers its column's 64 codes (four 8-byte loads), makes exact
+//               gathers its column's 64 codes (four 8-byte loads from a rotated
+//               start lane: no bank conflicts), makes exact
 //               q, multiplies by the group scale (rounded to the activation
 //               type, as the tensor-core operand must be) and stores 32 packed
 //               pairs to an 8-deep ring of A buffers in tensor memory; after a
@@ -43,7 +44,7 @@ namespace {
 constexpr int TM = 128;  // output columns per tile (MMA M)
 constexpr int TN = 256;  // tokens per tile (MMA N)
 constexpr int BK = 64;
-constexpr int kStages = 5;
+constexpr int kStages = 6;
 constexpr int kABufs = 8;
 constexpr int kDqWarps = 8;
 constexpr int kProdWarp = 8;
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
         const int cl = 32 * q + lane;  // column within the strip group = TMEM lane
         const int sl = cl >> 4;        // strip
         const int c = lane & 15, g = c & 7, hh = c >> 3;
+        const int rot = WBITS == 4 ? (g >> 1) : ((g >> 2) + 2 * (lane >> 4));  // bank-conflict-free gather
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         OT* C = reinterpret_cast<OT*>(p.C);
         bool ok = true;
@@ -215,12 +217,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                     s2 = v | (v << 16);
                 }
                 const uint32_t ta = tmem + lane_base + kColA + 32u * ab;
+                uint32_t cw[WBITS == 4 ? 8 : 4];  // this column's codes, k order
+                if constexpr (WBITS == 4) gather_column_u4(codes, g, hh, rot, valid, cw);
+                else gather_column_t2(codes, g, hh, rot, valid, cw);
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     uint32_t r[8];
                     if constexpr (WBITS == 4) {
-                        uint2 w = make_uint2(0u, 0u);
-                        if (valid) w = *reinterpret_cast<const uint2*>(codes + (4 * g + t) * 16 + 8 * hh);
+                        const uint2 w = make_uint2(cw[2 * t], cw[2 * t + 1]);
                         uint32_t lo[4], hi[4];
                         if constexpr (kBF16) {
                             dequant_u4_bf16(w.x, lo);
@@ -235,8 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                             r[4 + e] = mul2<kBF16>(hi[e], s2);
                         }
                     } else {
-                        uint32_t w = 0u;
-                        if (valid) w = *reinterpret_cast<const uint32_t*>(codes + (4 * g + t) * 8 + 4 * hh);
+                        const uint32_t w = cw[t];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) r[e] = mul2<kBF16>(dequant_t2_pair<kBF16>(w, e), s2);
                     }
