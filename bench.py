@@ -313,6 +313,38 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
                    for n, _, _ in tp.LAYER_SHAPES)
     ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
 
+    # The all-reduce after O and down: hq_allreduce_sum over NVLink peer memory
+    # (the row-parallel outputs live in PyTorch symmetric memory), or NCCL.
+    use_hq = world > 1 and args.stack_comm == "hq"
+    epoch = [0]
+    if use_hq:
+        import ctypes
+        import torch.distributed._symmetric_memory as symm
+        flags = symm.empty(32, dtype=torch.int32, device=dev)
+        flags.zero_()
+        hf = symm.rendezvous(flags, dist.group.WORLD)
+        fptrs = (ctypes.c_void_p * world)(*hf.buffer_ptrs)
+        peers = {}
+        for name in tp.ROW_PARALLEL:
+            buf = symm.empty((rows, specs[name].N), dtype=torch.bfloat16, device=dev)
+            hb = symm.rendezvous(buf, dist.group.WORLD)
+            Y[name] = buf
+            mc = int(hb.multicast_ptr or 0) if args.nvls else 0
+            peers[name] = ((ctypes.c_void_p * world)(*hb.buffer_ptrs), hb, ctypes.c_void_p(mc))
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    def all_reduce(name):
+        if use_hq:
+            epoch[0] += 1
+            st = L.hq_allreduce_sum(peers[name][0], fptrs, peers[name][2], world, rank, _lib.HQ_BF16,
+                                    Y[name].numel(), epoch[0], args.ar_ctas, ctypes.c_void_p(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        else:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(Y[name])
+
     def step():
         for layer in range(layers):
             for name, _, _ in tp.LAYER_SHAPES:
@@ -321,7 +353,7 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
                 _gemm_call(L, _lib, X[name], _lib.HQ_BF16, Wt, _lib.HQ_WFMT_TILE_U4, St, _lib.HQ_BF16, Y[name],
                            _lib.HQ_BF16, rows, sp.N, sp.K, ws, stream)
                 if sp.row_parallel and world > 1:
-                    dist.all_reduce(Y[name])
+                    all_reduce(name)
 
     with torch.cuda.stream(stream):
         for _ in range(2):
@@ -345,14 +377,24 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
         dist.barrier()
     flop = 2.0 * rows * sum(K * N for _, K, N in tp.LAYER_SHAPES) * layers
     tf = flop / (ms / 1e3) / 1e12
+    collective = None
+    if world > 1:
+        collective = "NCCL all_reduce"
+        if use_hq:
+            collective = ("hq_allreduce_sum, NVLS multicast (multimem)" if any(v[2].value for v in peers.values())
+                          else "hq_allreduce_sum, NVLink peer loads")
+            torch.cuda.synchronize()
+            dist.barrier()
+            peers.clear()
     del W, X, Y, ws
     torch.cuda.empty_cache()
     return {"metric": "TP layer-stack TFLOP/s (BASELINE configs[4])", "value": tf, "unit": "TFLOP/s",
             "tokens_per_s": rows / (ms / 1e3), "ms_per_step": ms, "n_gpus": world, "layers": layers,
             "rows_per_step": rows, "scaling": "strong", "dtype": "bf16",
             "frac_of_n_x_peak": tf / (world * peaks["bf16_tflops"]),
+            "collective": collective,
             "timing": f"{steps} steps after 2 warm-up, CUDA events on the compute stream, max over ranks; "
-                      "64 x 4 hq_gemm launches + 128 NCCL all-reduces per step at TP"}
+                      "64 x 4 hq_gemm launches + 128 all-reduces per step at TP"}
 
 
 def run_case(args):
@@ -395,6 +437,9 @@ def main():
                     help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits")
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
+    ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")
+    ap.add_argument("--ar-ctas", type=int, default=128, help="CTAs of hq_allreduce_sum")
+    ap.add_argument("--no-nvls", dest="nvls", action="store_false", help="hq_allreduce_sum without NVLink multicast")
     ap.add_argument("--prefill-ms", default="512,2048,8192", help="token counts of the prefill sweep")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -194,6 +194,30 @@ HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
 HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
                                      int K, int N, hq_stream_t stream);
 
+/*
+ * In-place sum over the `world` GPUs of one node (tensor-parallel all-reduce of
+ * the row-parallel GEMM outputs), through peer memory over NVLink.
+ *   peer_bufs[j]:  rank j's buffer of `count` HQ_BF16 / HQ_F16 elements, as
+ *                  addressable from this GPU (peer-mapped memory, e.g. PyTorch
+ *                  symmetric memory); host array of `world` device addresses.
+ *   peer_flags[j]: rank j's flag area, 32 zero-initialised uint32 (peer-mapped).
+ *   multicast:     NVLink multicast (NVLS) address of the buffers, or NULL.  With
+ *                  it the switch sums (multimem.ld_reduce, fp32 accumulation)
+ *                  and broadcasts (multimem.st): each rank moves 2/world of the
+ *                  vector over NVLink instead of 2 (world-1)/world.
+ *   epoch:         1 for the first call on these flags, +1 for every call after.
+ *   ctas:          CTAs per call (the same on every call with these flags).
+ * Every rank makes the same calls in the same order on its own stream; on
+ * return every buffer holds the sum (fp32 accumulation; every rank holds the
+ * same bits: in rank order 0..world-1 without multicast, in the switch's order
+ * with it).  Waits for peers are bounded: a rank that never
+ * arrives makes the others record HQ_ERR_TIMEOUT (hq_check_device_error).
+ * No counterpart in the reference (it has no multi-GPU path).
+ */
+HQ_API hq_status hq_allreduce_sum(void* const* peer_bufs, unsigned* const* peer_flags, void* multicast,
+                                  int world, int rank, hq_dtype dtype, size_t count, unsigned epoch, int ctas,
+                                  hq_stream_t stream);
+
 /* Turn the launch overlap described at hq_gemm on (1, default) or off (0)
  * for the whole process. */
 HQ_API void hq_set_launch_overlap(int enable);

@@ -37,6 +37,7 @@ SIGNATURES = {
     "hq_tq1_0_to_tile_t2": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "hq_check_device_error": (_i, []),
     "hq_set_launch_overlap": (None, [_i]),
+    "hq_allreduce_sum": (_i, [_vp, _vp, _vp, _i, _i, _i, _sz, _u32, _i, _vp]),
     "hq_marlin_engine_create": (_vp, [_u32, _u32, _u32, _u32]),
     "hq_marlin_engine_destroy": (None, [_vp]),
     "hq_marlin_repack_q4k_to_marlin": (_i, [_vp, _vp, _vp, _u32, _u32, ctypes.POINTER(_d)]),
