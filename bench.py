@@ -36,6 +36,7 @@ sys.path.insert(0, ROOT)
 SHAPES = [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816), ("down", 17408, 5120)]
 MS = [1, 2, 4, 8, 16]
 GROUP = 128
+L2_BYTES = 126 * 1024 * 1024  # B200 L2
 METRIC = "W4A16 GEMM weight TB/s (M≤16) & TFLOPS (M≥1024) at 1–8 B200 vs roofline"
 
 
@@ -230,6 +231,58 @@ def prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args):
             "timing": "per GEMM: CUDA events around 10 launches (4 at M=8192) after 3 warm-up, 2 rotating weight "
                       "copies; value = total FLOP / total time",
             "per_gemm": rows}
+
+
+def tq1_sweep(torch, L, _lib, dev, stream, peaks, args):
+    """The reference decoder's own ternary path: hq_tq1_0_gemv (drop-in for kernel_gemv_tq1_0,
+    native_decoder.cu:155-206; fp32 x, M = 1) on TQ1_0 blocks (56 B per 256 weights) at the output
+    projection (vocab 248320 x hidden 5120, native_decoder.hpp:180) and the four 27B layer shapes.
+    GB/s of TQ1_0 bytes.  Each shape rotates enough weight copies that every timed launch reads a copy
+    last touched more than 2 L2 sizes earlier."""
+    import ctypes
+    vp = ctypes.c_void_p
+    g = torch.Generator(device=dev)
+    g.manual_seed(321)
+    rows, tot_b, tot_ms = [], 0.0, 0.0
+    for name, K, N in [("output_proj", 5120, 248320)] + SHAPES:
+        nbytes = N * (K // 256) * 56
+        n_copies = min(64, max(2, -(-int(2.5 * L2_BYTES) // nbytes) + 1))
+        W = torch.randint(0, 243, (n_copies, N, K // 256, 56), dtype=torch.uint8, device=dev, generator=g)
+        d = (torch.rand((n_copies, N, K // 256), device=dev, generator=g) * 0.04 + 0.01).half()
+        W[..., 0:2] = d.view(torch.uint8).view(n_copies, N, K // 256, 2)
+        W[..., 54:56] = 0
+        W = W.view(n_copies, -1)
+        x = torch.randn(K, device=dev, generator=g)
+        out = torch.empty(N, device=dev)
+
+        def fn(c):
+            st = L.hq_tq1_0_gemv(vp(x.data_ptr()), vp(W[c].data_ptr()), vp(out.data_ptr()), K, N,
+                                 vp(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        reps = max(10, n_copies)
+        with torch.cuda.stream(stream):
+            for c in range(3):
+                fn(n_copies - 1 - c)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for r in range(reps):
+                fn(r % n_copies)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        rows.append({"shape": name, "K": K, "N": N, "copies": n_copies, "us": round(ms * 1e3, 2),
+                     "GBps": round(nbytes / (ms / 1e3) / 1e9, 1)})
+        tot_b += nbytes
+        tot_ms += ms
+        del W, d
+    gbps = tot_b / (tot_ms / 1e3) / 1e9
+    return {"metric": "TQ1_0 GEMV GB/s (M=1, fp32 x)", "value": gbps, "unit": "GB/s",
+            "frac_hbm": gbps / peaks["hbm_gbs"], "per_gemv": rows,
+            "timing": "per shape: CUDA events around max(10, copies) launches after 3 warm-up launches on "
+                      "other copies; launch gaps included"}
 
 
 def _ternary_tile(torch, nbytes, dev, g):
@@ -647,10 +700,11 @@ def main():
         stack = tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args)
         hq.check_device_error()
 
-    prefill = ternary = None
+    prefill = ternary = tq1 = None
     if world == 1 and not args.no_extra:
         prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
         ternary = ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
+        tq1 = tq1_sweep(torch, L, _lib, dev, stream, peaks, args)
         hq.check_device_error()
 
     cpu = None
@@ -695,6 +749,8 @@ def main():
             line["prefill"] = prefill
         if ternary is not None:
             line["ternary"] = ternary
+        if tq1 is not None:
+            line["tq1_0"] = tq1
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

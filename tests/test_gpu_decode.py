@@ -206,12 +206,81 @@ def test_tq1_0_to_tile_t2_then_gemm(K, N):
     assert o.max_rel_err(y2.cpu().numpy()[0], ref2) <= TOL["f16"]
 
 
-@pytest.mark.parametrize("K,N", [(5120, 7168), (17408, 5120)])
-def test_tq1_0_gemv_full_size(K, N):
-    rng = np.random.default_rng(K)
+@pytest.mark.parametrize("K,N", [(1024, 1), (1024, 45), (2048, 100), (768, 37), (4096, 4097)])
+def test_tq1_0_gemv_edge_shapes(K, N):
+    """Tensor-core path (K % 1024 == 0) with ragged row counts, and the row-per-warp path (K = 768);
+    non-finite block scales and malformed bytes (>= 243) follow the reference's digit arithmetic."""
+    rng = np.random.default_rng(K + N)
+    t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+    d[0, 0] = 0x7E00  # NaN
+    d[N - 1, K // 256 - 1] = 0xFC00  # -Inf
+    blob = o.pack_tq1_0(t, d).reshape(N, -1)
+    blob[:, 2:54:9] = 250  # bytes outside 0..242
+    blob = blob.ravel()
+    x = rng.standard_normal(K).astype(np.float32)
+    ref = o.gemv_tq1_0(x, blob, K, N)
+    y = hq.tq1_0_gemv(cuda(x, "f32"), cuda(blob, None), N)
+    torch.cuda.synchronize()
+    assert o.max_rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+def test_tq1_0_gemv_x_offset_by_one_float():
+    """x only 4-byte aligned (a view one float into a buffer) takes the scalar staging loop."""
+    K, N = 1024, 64
+    rng = np.random.default_rng(11)
     t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
     d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
     blob = o.pack_tq1_0(t, d)
+    x = rng.standard_normal(K + 1).astype(np.float32)
+    y = hq.tq1_0_gemv(cuda(x, "f32")[1:], cuda(blob, None), N)
+    assert o.max_rel_err(y.cpu().numpy(), o.gemv_tq1_0(x[1:], blob, K, N)) <= 1e-5
+
+
+@pytest.mark.parametrize("kind", ["zero", "tiny", "huge", "nonfinite"])
+def test_tq1_0_gemv_x_ranges(kind):
+    """x = 0, x near the fp32 minimum, x near the fp32 maximum, and x holding Inf/NaN (the float path)."""
+    K, N = 2048, 96
+    rng = np.random.default_rng(7)
+    t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+    blob = o.pack_tq1_0(t, d)
+    x = rng.standard_normal(K).astype(np.float32)
+    if kind == "zero":
+        x[:] = 0
+    elif kind == "tiny":
+        x *= np.float32(1e-37)
+    elif kind == "huge":
+        x *= np.float32(1e30)
+    else:
+        x[5] = np.inf
+        x[700] = np.nan
+    ref = o.gemv_tq1_0(x, blob, K, N)
+    y = hq.tq1_0_gemv(cuda(x, "f32"), cuda(blob, None), N).cpu().numpy()
+    if kind == "nonfinite":
+        assert np.array_equal(np.isnan(y), np.isnan(ref)) and np.array_equal(np.isinf(y), np.isinf(ref))
+        fin = np.isfinite(ref)
+        assert np.allclose(y[fin], ref[fin], rtol=1e-5, atol=1e-5)
+    elif kind == "zero":
+        assert np.array_equal(y, np.zeros_like(y))
+    else:
+        assert o.max_rel_err(y, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("K,N", [(5120, 7168), (17408, 5120), (5120, 248320)])
+def test_tq1_0_gemv_full_size(K, N):
+    """The layer shapes and the output projection (vocab 248320 x hidden 5120)."""
+    rng = np.random.default_rng(K)
+    if N * K <= 100_000_000:
+        t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+        d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+        blob = o.pack_tq1_0(t, d)
+    else:  # well-formed blocks drawn directly as bytes: packed values 0..242, d ~ U(0.01, 0.05), pad 0
+        blk = rng.integers(0, 243, size=(N, K // 256, 56), dtype=np.uint8)
+        d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint8).reshape(N, K // 256, 2)
+        blk[:, :, 0:2] = d
+        blk[:, :, 54:56] = 0
+        blob = blk.ravel()
     x = rng.standard_normal(K).astype(np.float32)
     ref = o.gemv_tq1_0(x, blob, K, N)
     y = hq.tq1_0_gemv(cuda(x, "f32"), cuda(blob, None), N)
