@@ -221,6 +221,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint32_t s_max[kTcWarps];
     __shared__ int s_bad[kTcWarps];
+    __shared__ float s_part[kTcWarps][2][16];  // partial-unit row sums of a chunk (head, tail of each run)
+    __shared__ int s_part_unit[kTcWarps][2];
     const uint8_t* lut = smem;                                    // digit table
     uint2* btab = reinterpret_cast<uint2*>(smem + kSmemB);       // [window of chunk][mma][lane]
     float4* qtab = reinterpret_cast<float4*>(smem + kSmemQ);     // [block of chunk] (Q0*128+Q1, Q2*128+Q3, -, -)
@@ -274,23 +276,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     frexpf(__uint_as_float(m), &e);  // max|x| < 2^e (e = 0 when x == 0)
     const int sh = 27 - e;
 
-    // 2. this warp's steps: its units (every kTcWarps-th 16-row unit of the CTA's range) x groups,
-    //    chunk by chunk (all units' groups of chunk 0, then of chunk 1, ...); the ring runs two
-    //    steps ahead of the decode.
+    // 2. work: the CTA's 16-row units [u_begin, u_begin + u_count).  Per chunk of kChunkGroups groups,
+    //    the tasks (unit, group) in unit-major order are cut into kTcWarps contiguous runs, one per warp.
+    //    The ring runs two tasks ahead of the decode, across chunk boundaries.
     const int n_units = (out_dim + 15) / 16;
     const int per_cta = (n_units + gridDim.x - 1) / gridDim.x;
     const int u_begin = blockIdx.x * per_cta;
     const int u_count = max(0, min(per_cta, n_units - u_begin));
-    const int my_units = u_count > warp ? (u_count - warp + kTcWarps - 1) / kTcWarps : 0;
-    const int n_steps = my_units * n_groups;
-    const int full_chunk_steps = my_units * kChunkGroups;
+    const int n_chunks = (n_groups + kChunkGroups - 1) / kChunkGroups;
+    auto chunk_groups = [&](int c) { return min(kChunkGroups, n_groups - c * kChunkGroups); };
+    auto run_of = [&](int c, int& t0, int& t1) {  // this warp's tasks of chunk c: [t0, t1)
+        const int total = u_count * chunk_groups(c);
+        const int T = (total + kTcWarps - 1) / kTcWarps;
+        t0 = min(warp * T, total);
+        t1 = min(t0 + T, total);
+    };
+    int n_steps = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+        int a, b;
+        run_of(c, a, b);
+        n_steps += b - a;
+    }
     uint8_t* ring = smem + kSmemRing + warp * 2 * kStageBytes;
     bool ok = true;
-    auto issue = [&](int st) {  // request step st into stage st & 1
-        const int c = st / full_chunk_steps, r = st - c * full_chunk_steps;
-        const int n_cg = min(kChunkGroups, n_groups - c * kChunkGroups);
-        const int unit = u_begin + warp + (r / n_cg) * kTcWarps;
-        const int G = c * kChunkGroups + r % n_cg;
+    int i_chunk = 0, i_task = 0, i_end = 0, i_unit = 0, i_grp = 0;  // issue cursor: next task to request
+    run_of(0, i_task, i_end);
+    i_unit = i_task / chunk_groups(0);
+    i_grp = i_task - i_unit * chunk_groups(0);
+    auto issue = [&](int st) {  // request the next task into stage st & 1 (st < n_steps)
+        while (i_task == i_end && i_chunk + 1 < n_chunks) {
+            ++i_chunk;
+            run_of(i_chunk, i_task, i_end);
+            i_unit = i_task / chunk_groups(i_chunk);
+            i_grp = i_task - i_unit * chunk_groups(i_chunk);
+        }
+        const int unit = u_begin + i_unit;
+        const int G = i_chunk * kChunkGroups + i_grp;
+        ++i_task;
+        if (++i_grp == chunk_groups(i_chunk)) i_grp = 0, ++i_unit;
         const int rows = min(16, out_dim - unit * 16);
         uint64_t* bar = &bars[2 * warp + (st & 1)];
         if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(rows * kGroupBytes));
@@ -363,84 +386,125 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncthreads();
 
-        // 5. decode this chunk's steps
-        for (int k = 0; k < my_units; ++k) {
-            const int unit = u_begin + warp + k * kTcWarps;
-            float y[2] = {0.f, 0.f};
-            float dsc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // block scale per parity and row
-            int acc[4] = {0, 0, 0, 0};
-            for (int Gl = 0; Gl < n_cg; ++Gl, ++st) {
-                if (ok) ok = mbar_wait(&bars[2 * warp + (st & 1)], (uint32_t)((st >> 1) & 1), err);
-                const uint32_t sp = smem_u32(ring + (st & 1) * kStageBytes + 8 * t);
+        // 5. decode this warp's run of the chunk's tasks.  Row sums stay in registers while the unit
+        //    is the same; a segment that covers the unit's whole chunk is added to out directly, a
+        //    partial one (only at the run's head or tail) goes to s_part and is combined below.
+        int t0, t1;
+        run_of(c, t0, t1);
+        if (lane == 0) s_part_unit[warp][0] = s_part_unit[warp][1] = -1;
+        float y[2] = {0.f, 0.f};
+        int seg_unit = -1, seg_start = t0;
+        auto emit = [&](int seg_end) {  // tasks [seg_start, seg_end) of unit seg_unit
+            const bool full = seg_start == seg_unit * n_cg && seg_end == seg_unit * n_cg + n_cg;
+            const int slot = seg_start == t0 ? 0 : 1;
 #pragma unroll
-                for (int win = 0; win < 7; ++win) {
-                    uint2 wv[2];
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)
-                        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(wv[q].x), "=r"(wv[q].y)
-                            : "r"(sp + (g + 8 * q) * kGroupBytes + 32 * win));
-                    if (win == 0 || win == 1 || win == 3 || win == 5) {  // a block starts: take its d
-                        const int blk = win == 0 ? 0 : win == 1 ? 1 : win == 3 ? 2 : 3;
-                        const int src = (lane & ~3) | (win == 0 ? 0 : win == 1 ? 3 : win == 3 ? 2 : 1);
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const uint32_t bits = __shfl_sync(0xffffffffu, wv[q].x, src);
-                            const float d = __half2float(__ushort_as_half((unsigned short)(bits & 0xFFFFu)));
-                            dsc[blk & 1][q] = fabsf(d) <= 65504.f ? d : 0.f;  // NaN/Inf: skipped, native_decoder.cu:174
-                        }
-                    }
-                    uint32_t R[2][10];  // A registers of rows g, g + 8
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        uint32_t T[8];
-#pragma unroll
-                        for (int beta = 0; beta < 8; ++beta) {
-                            const uint32_t word = beta < 4 ? wv[q].x : wv[q].y;
-                            const uint32_t off = __byte_perm(word, lane_off, 0x5504u | ((uint32_t)(beta & 3) << 4));
-                            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(T[beta]) : "r"(lut_s + off));
-                            R[q][beta] = T[beta] & 0x03030303u;
-                        }
-                        R[q][8] = (__byte_perm(__byte_perm(T[0], T[1], 0x0040), __byte_perm(T[2], T[3], 0x0040),
-                                               0x5410) >> 2) & 0x03030303u;
-                        R[q][9] = (__byte_perm(__byte_perm(T[4], T[5], 0x0040), __byte_perm(T[6], T[7], 0x0040),
-                                               0x5410) >> 2) & 0x03030303u;
-                    }
-                    const uint32_t bw = smem_u32(btab) + (uint32_t)((((Gl * 7 + win) * 5) * 32 + lane) * 8);
-#pragma unroll
-                    for (int mm = 0; mm < 5; ++mm) {
-                        uint2 b;
-                        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(b.x), "=r"(b.y) : "r"(bw + mm * 256));
-                        imma_u8s8(acc, R[0][2 * mm], R[1][2 * mm], R[0][2 * mm + 1], R[1][2 * mm + 1], b.x, b.y);
-                    }
-                    if (win == 1 || win == 3 || win == 5 || win == 6) {  // a block ends: fold it in
-                        const int blk = win == 1 ? 0 : win == 3 ? 1 : win == 5 ? 2 : 3;
-                        if (flush_even == ((blk & 1) == 0)) {
-                            const float2 qs = *reinterpret_cast<const float2*>(&qtab[4 * Gl + blk]);
-                            const float qf = (t & 1) ? qs.y : qs.x;
-#pragma unroll
-                            for (int q = 0; q < 2; ++q) {  // |C_p * 128 + C_{p+1}| < 2^23: exact in fp32
-                                const float v = (float)(acc[2 * q] * 128 + acc[2 * q + 1]) - qf;
-                                y[q] = fmaf(dsc[blk & 1][q], v, y[q]);
-                                acc[2 * q] = 0;
-                                acc[2 * q + 1] = 0;
-                            }
-                        }
-                    }
-                }
-                __syncwarp();  // every lane is done with this stage
-                if (ok && st + 2 < n_steps) issue(st + 2);
-            }
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {  // sum the four lanes of each row; chunks add up in out
+            for (int q = 0; q < 2; ++q) {
                 float v = ldexpf(y[q], lane_scale_exp);
                 v += __shfl_xor_sync(0xffffffffu, v, 1);
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
-                const int row = unit * 16 + g + 8 * q;
-                if (t == 0 && row < out_dim) {
-                    const float part = ldexpf(v, e - 27);
-                    out[row] = c == 0 ? part : out[row] + part;
+                v = ldexpf(v, e - 27);
+                const int row = (u_begin + seg_unit) * 16 + g + 8 * q;
+                if (t == 0) {
+                    if (!full)
+                        s_part[warp][slot][g + 8 * q] = v;
+                    else if (row < out_dim)
+                        out[row] = c == 0 ? v : out[row] + v;
+                }
+                y[q] = 0.f;
+            }
+            if (!full && lane == 0) s_part_unit[warp][slot] = seg_unit;
+        };
+        int ul = t0 / max(n_cg, 1), Gl = t0 - ul * n_cg;  // task = ul * n_cg + Gl
+        for (int task = t0; task < t1; ++task, ++st, (++Gl == n_cg ? (Gl = 0, ++ul) : 0)) {
+            if (ul != seg_unit) {
+                if (seg_unit >= 0) emit(task);
+                seg_unit = ul;
+                seg_start = task;
+            }
+            float dsc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // block scale per parity and row
+            int acc[4] = {0, 0, 0, 0};
+            if (ok) ok = mbar_wait(&bars[2 * warp + (st & 1)], (uint32_t)((st >> 1) & 1), err);
+            const uint32_t sp = smem_u32(ring + (st & 1) * kStageBytes + 8 * t);
+#pragma unroll
+            for (int win = 0; win < 7; ++win) {
+                uint2 wv[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(wv[q].x), "=r"(wv[q].y)
+                        : "r"(sp + (g + 8 * q) * kGroupBytes + 32 * win));
+                if (win == 0 || win == 1 || win == 3 || win == 5) {  // a block starts: take its d
+                    const int blk = win == 0 ? 0 : win == 1 ? 1 : win == 3 ? 2 : 3;
+                    const int src = (lane & ~3) | (win == 0 ? 0 : win == 1 ? 3 : win == 3 ? 2 : 1);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint32_t bits = __shfl_sync(0xffffffffu, wv[q].x, src);
+                        const float d = __half2float(__ushort_as_half((unsigned short)(bits & 0xFFFFu)));
+                        dsc[blk & 1][q] = fabsf(d) <= 65504.f ? d : 0.f;  // NaN/Inf: skipped, native_decoder.cu:174
+                    }
+                }
+                uint32_t R[2][10];  // A registers of rows g, g + 8
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    uint32_t T[8];
+#pragma unroll
+                    for (int beta = 0; beta < 8; ++beta) {
+                        const uint32_t word = beta < 4 ? wv[q].x : wv[q].y;
+                        const uint32_t off = __byte_perm(word, lane_off, 0x5504u | ((uint32_t)(beta & 3) << 4));
+                        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(T[beta]) : "r"(lut_s + off));
+                        R[q][beta] = T[beta] & 0x03030303u;
+                    }
+                    R[q][8] = (__byte_perm(__byte_perm(T[0], T[1], 0x0040), __byte_perm(T[2], T[3], 0x0040),
+                                           0x5410) >> 2) & 0x03030303u;
+                    R[q][9] = (__byte_perm(__byte_perm(T[4], T[5], 0x0040), __byte_perm(T[6], T[7], 0x0040),
+                                           0x5410) >> 2) & 0x03030303u;
+                }
+                const uint32_t bw = smem_u32(btab) + (uint32_t)((((Gl * 7 + win) * 5) * 32 + lane) * 8);
+#pragma unroll
+                for (int mm = 0; mm < 5; ++mm) {
+                    uint2 b;
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(b.x), "=r"(b.y) : "r"(bw + mm * 256));
+                    imma_u8s8(acc, R[0][2 * mm], R[1][2 * mm], R[0][2 * mm + 1], R[1][2 * mm + 1], b.x, b.y);
+                }
+                if (win == 1 || win == 3 || win == 5 || win == 6) {  // a block ends: fold it in
+                    const int blk = win == 1 ? 0 : win == 3 ? 1 : win == 5 ? 2 : 3;
+                    if (flush_even == ((blk & 1) == 0)) {
+                        const float2 qs = *reinterpret_cast<const float2*>(&qtab[4 * Gl + blk]);
+                        const float qf = (t & 1) ? qs.y : qs.x;
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {  // |C_p * 128 + C_{p+1}| < 2^23: exact in fp32
+                            const float v = (float)(acc[2 * q] * 128 + acc[2 * q + 1]) - qf;
+                            y[q] = fmaf(dsc[blk & 1][q], v, y[q]);
+                            acc[2 * q] = 0;
+                            acc[2 * q + 1] = 0;
+                        }
+                    }
                 }
             }
+            __syncwarp();  // every lane is done with this stage
+            if (ok && st + 2 < n_steps) issue(st + 2);
+        }
+        if (seg_unit >= 0) emit(t1);
+        __syncthreads();
+        if (warp == 0 && lane < 16) {  // partial segments, unit by unit in warp order (deterministic)
+            int cur = -1;
+            float sum = 0.f;
+            auto put = [&]() {
+                const int row = (u_begin + cur) * 16 + lane;
+                if (row < out_dim) out[row] = c == 0 ? sum : out[row] + sum;
+            };
+            for (int ww = 0; ww < kTcWarps; ++ww)
+#pragma unroll
+                for (int sl = 0; sl < 2; ++sl) {
+                    const int u = s_part_unit[ww][sl];
+                    if (u < 0) continue;
+                    if (u != cur) {
+                        if (cur >= 0) put();
+                        cur = u;
+                        sum = 0.f;
+                    }
+                    sum += s_part[ww][sl][lane];
+                }
+            if (cur >= 0) put();
         }
     }
 }
@@ -494,7 +558,7 @@ cudaError_t launch_tq1_0_gemv(const float* x, const uint8_t* w, float* out, int 
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const DeviceInfo& di = device_info(dev);
-    if (in_dim % 1024 == 0 && (size_t)kTcSmemBytes + 1024 <= di.smem_optin && (reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
+    if (in_dim % 1024 == 0 && (size_t)kTcSmemBytes + 4096 <= di.smem_optin && (reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
         e = ensure_smem_attr(reinterpret_cast<const void*>(tq1_0_gemv_tc_kernel), dev, kTcSmemBytes);
         if (e != cudaSuccess) return e;
         const int units = (out_dim + 15) / 16;
