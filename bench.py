@@ -455,11 +455,26 @@ def run_case(args):
     import torch
     from nebula_b200 import _lib, hq
     f = args.case.split(",")
+    dev = torch.device("cuda", 0)
+    if f[0] == "tq1":  # tq1,K,N: hq_tq1_0_gemv on well-formed TQ1_0 blocks (packed 0..242, d ~ U(0.01, 0.05))
+        K, N = int(f[1]), int(f[2])
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        W = torch.randint(0, 243, (N, K // 256, 56), dtype=torch.uint8, device=dev, generator=g)
+        d = (torch.rand((N, K // 256), device=dev, generator=g) * 0.04 + 0.01).half()
+        W[..., 0:2] = d.view(torch.uint8).view(N, K // 256, 2)
+        W[..., 54:56] = 0
+        x = torch.randn(K, device=dev, generator=g)
+        for _ in range(args.steps):
+            y = hq.tq1_0_gemv(x, W.view(-1), N)
+        torch.cuda.synchronize()
+        hq.check_device_error()
+        print(json.dumps({"case": args.case, "checksum": float(y.abs().sum())}))
+        return 0
     K, N, M = int(f[0]), int(f[1]), int(f[2])
     dt = f[3] if len(f) > 3 else "f16"
     wfmt = _lib.HQ_WFMT_TILE_T2 if len(f) > 4 and f[4] == "t2" else _lib.HQ_WFMT_TILE_U4
     tdt = torch.float16 if dt == "f16" else torch.bfloat16
-    dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(5)
     W = torch.randint(0, 256, (hq.weight_bytes(wfmt, K, N),), dtype=torch.uint8, device=dev, generator=g)
@@ -487,7 +502,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill and ternary sweeps")
     ap.add_argument("--no-stack", action="store_true", help="skip the TP layer stack (configs[4])")
     ap.add_argument("--case", default=None,
-                    help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits")
+                    help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits; "
+                         "'tq1,K,N' runs hq_tq1_0_gemv instead")
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")

@@ -182,6 +182,10 @@ HQ_API hq_status hq_repack_device(const void* src, hq_wfmt src_fmt, void* dst, h
  *   out[row] = sum_b sum_j d_b * trit_j * x[256b + j]; blocks with NaN/Inf d
  *   are skipped.  x, out fp32; w = [out_dim][in_dim/256] TQ1_0 blocks.
  * Replaces kernel_gemv_tq1_0 (native_decoder.cu:155-206), computing every row.
+ * in_dim % 1024 == 0 with w 16-byte aligned takes the tensor-core kernel (x as
+ * a 28-bit fixed-point copy relative to max|x|: results within 1e-5 of max|out|
+ * of the fp32 loop, deterministic); other shapes, and any x holding NaN/Inf,
+ * take the fp32 loop.  Requires w 8-byte and x 4-byte aligned.
  */
 HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
                                int in_dim, int out_dim, hq_stream_t stream);
