@@ -285,6 +285,45 @@ def tq1_sweep(torch, L, _lib, dev, stream, peaks, args):
                       "other copies; launch gaps included"}
 
 
+def proj_sweep(torch, L, _lib, dev, stream, peaks, args):
+    """The output projection over GGML BF16 / Q8_0 / F32 rows (kernel_output_projection,
+    forward_baseline.cu:178-257; TQ1_0 rows are the tq1_0 sub-object) at vocab 248320 x hidden 5120,
+    fp32 x: GB/s of weight bytes, two rotating weight copies (each larger than L2)."""
+    import ctypes
+    vp = ctypes.c_void_p
+    K, N = 5120, 248320
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    rows = []
+    for name, w_type in (("bf16", _lib.HQ_GGML_BF16), ("q8_0", _lib.HQ_GGML_Q8_0), ("f32", _lib.HQ_GGML_F32)):
+        if w_type == _lib.HQ_GGML_Q8_0:
+            W = torch.randint(-128, 128, (2, N, K // 32, 34), dtype=torch.int8, device=dev, generator=g).view(torch.uint8)
+            d = (torch.rand((2, N, K // 32), device=dev, generator=g) * 0.015 + 0.005).half()
+            W[..., 0:2] = d.view(torch.uint8).view(2, N, K // 32, 2)
+            del d
+        elif w_type == _lib.HQ_GGML_BF16:
+            W = torch.randn((2, N, K), device=dev, generator=g).bfloat16().view(torch.uint8)
+        else:
+            W = torch.randn((2, N, K), device=dev, generator=g).view(torch.uint8)
+        W = W.reshape(2, -1)
+        x = torch.randn(K, device=dev, generator=g)
+        out = torch.empty(N, device=dev)
+
+        def fn(c):
+            st = L.hq_output_projection(vp(x.data_ptr()), vp(W[c].data_ptr()), w_type, vp(out.data_ptr()), K, N,
+                                        vp(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        ms = _time_launches(torch, stream, fn, 2, reps=10)
+        nbytes = W.shape[1]
+        rows.append({"type": name, "K": K, "N": N, "weight_bytes": nbytes, "us": round(ms * 1e3, 1),
+                     "GBps": round(nbytes / (ms / 1e3) / 1e9, 1),
+                     "frac_hbm": round(nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 3)})
+        del W
+    return {"metric": "output projection GEMV GB/s (vocab 248320 x 5120, M=1, fp32 x)", "per_type": rows,
+            "timing": "CUDA events around 10 launches after 3 warm-up, 2 rotating weight copies"}
+
+
 def _ternary_tile(torch, nbytes, dev, g):
     f = torch.randint(0, 3, (nbytes, 4), dtype=torch.uint8, device=dev, generator=g)
     return (f[:, 0] | (f[:, 1] << 2) | (f[:, 2] << 4) | (f[:, 3] << 6)).contiguous()
@@ -716,11 +755,12 @@ def main():
         stack = tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args)
         hq.check_device_error()
 
-    prefill = ternary = tq1 = None
+    prefill = ternary = tq1 = proj = None
     if world == 1 and not args.no_extra:
         prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
         ternary = ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
         tq1 = tq1_sweep(torch, L, _lib, dev, stream, peaks, args)
+        proj = proj_sweep(torch, L, _lib, dev, stream, peaks, args)
         hq.check_device_error()
 
     cpu = None
@@ -767,6 +807,8 @@ def main():
             line["ternary"] = ternary
         if tq1 is not None:
             line["tq1_0"] = tq1
+        if proj is not None:
+            line["output_projection"] = proj
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

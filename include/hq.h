@@ -198,6 +198,38 @@ HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
 HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
                                      int K, int N, hq_stream_t stream);
 
+/* GGML tensor type ids of the projection weights (gguf_parser.hpp:33-64). */
+#define HQ_GGML_F32 0
+#define HQ_GGML_Q8_0 8
+#define HQ_GGML_BF16 30
+#define HQ_GGML_TQ1_0 34
+#define HQ_GGML_TQ1_0_ALT 143 /* read as TQ1_0, as forward_baseline.cu:82,218 do */
+
+/*
+ * Output projection: logits[row] = dot(W[row, :], x), fp32 x [embedding_dim],
+ * fp32 logits [vocab_size].  W rows by w_type: HQ_GGML_F32 / HQ_GGML_BF16
+ * embedding_dim elements; HQ_GGML_Q8_0 embedding_dim/32 blocks of 34 bytes
+ * (fp16 d + 32 int8, d applied unchecked); HQ_GGML_TQ1_0 (or _ALT)
+ * embedding_dim/256 TQ1_0 blocks, computed by hq_tq1_0_gemv.
+ * Replaces kernel_output_projection (forward_baseline.cu:178-257) and its
+ * launch (:489-499).  Fast paths: F32 with embedding_dim % 4 == 0 and W
+ * 16-byte aligned, BF16 with embedding_dim % 8 == 0 and W 16-byte aligned,
+ * Q8_0 with embedding_dim % 64 == 0 and W 4-byte aligned; other shapes run the
+ * reference's own lane loop.  x 4-byte aligned.  No workspace.
+ */
+HQ_API hq_status hq_output_projection(const float* x, const void* w, int w_type, float* logits,
+                                      int embedding_dim, int vocab_size, hq_stream_t stream);
+
+/*
+ * Embedding row lookup: out[i] = W[token_id, i] as fp32 (Q8_0: d * q; TQ1_0:
+ * d * trit with a NaN/Inf d read as 0).  Replaces kernel_embedding_lookup
+ * (forward_baseline.cu:55-109; native_decoder.cu:63-103 for TQ1_0).  Adds
+ * vocab_size, only to reject token_id outside [0, vocab_size) -- the reference
+ * reads out of bounds there.
+ */
+HQ_API hq_status hq_embedding_lookup(const void* table, int w_type, int token_id, float* out,
+                                     int embedding_dim, int vocab_size, hq_stream_t stream);
+
 /*
  * In-place sum over the `world` GPUs of one node (tensor-parallel all-reduce of
  * the row-parallel GEMM outputs), through peer memory over NVLink.

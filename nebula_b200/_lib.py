@@ -17,6 +17,7 @@ HQ_OK, HQ_ERR_INVALID_ARG, HQ_ERR_UNSUPPORTED_SHAPE, HQ_ERR_WORKSPACE_TOO_SMALL,
 HQ_F32, HQ_F16, HQ_BF16 = 0, 1, 2
 HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD, HQ_WFMT_TILE_U4, HQ_WFMT_LINEAR_T2, HQ_WFMT_TILE_T2, HQ_WFMT_TQ1_0 = range(6)
 HQ_NOALLOC_SCRATCH_BYTES = 64 << 20  # scratch array of hq_gemm_noalloc
+HQ_GGML_F32, HQ_GGML_Q8_0, HQ_GGML_BF16, HQ_GGML_TQ1_0, HQ_GGML_TQ1_0_ALT = 0, 8, 30, 34, 143
 
 STATUS_NAMES = {0: "HQ_OK", 1: "HQ_ERR_INVALID_ARG", 2: "HQ_ERR_UNSUPPORTED_SHAPE", 3: "HQ_ERR_WORKSPACE_TOO_SMALL",
                 4: "HQ_ERR_CUDA", 5: "HQ_ERR_TIMEOUT", 6: "HQ_ERR_MISALIGNED", 7: "HQ_ERR_UNSUPPORTED_DEVICE"}
@@ -35,6 +36,8 @@ SIGNATURES = {
     "hq_repack_device": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "hq_tq1_0_gemv": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "hq_tq1_0_to_tile_t2": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "hq_output_projection": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
+    "hq_embedding_lookup": (_i, [_vp, _i, _i, _vp, _i, _i, _vp]),
     "hq_check_device_error": (_i, []),
     "hq_set_launch_overlap": (None, [_i]),
     "hq_allreduce_sum": (_i, [_vp, _vp, _vp, _i, _i, _i, _sz, _u32, _i, _vp]),

@@ -45,14 +45,17 @@ const DeviceInfo& device_info(int dev) {
     return cache[dev];
 }
 
+// The attribute is a per-kernel maximum: keep the largest size set on each device and only
+// ever raise it, so that a launch with less shared memory never lowers it under another.
 cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes) {
     static std::mutex mu;
-    static std::set<std::pair<const void*, int>> done;
+    static std::map<std::pair<const void*, int>, int> set_max;
     std::lock_guard<std::mutex> lk(mu);
-    auto key = std::make_pair(fn, dev * 1000000 + bytes);
-    if (done.count(key)) return cudaSuccess;
+    const auto key = std::make_pair(fn, dev);
+    auto it = set_max.find(key);
+    if (it != set_max.end() && it->second >= bytes) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess) done.insert(key);
+    if (e == cudaSuccess) set_max[key] = bytes;
     return e;
 }
 
@@ -393,6 +396,49 @@ HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* sca
                                             static_cast<uint16_t*>(scales_f16), K, N,
                                             reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "tq1_0 conversion launch");
+}
+
+HQ_API hq_status hq_output_projection(const float* x, const void* w, int w_type, float* logits,
+                                      int embedding_dim, int vocab_size, hq_stream_t stream) {
+    if (!x || !w || !logits) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (embedding_dim <= 0 || vocab_size <= 0) return fail(HQ_ERR_INVALID_ARG, "bad size");
+    const bool tq1 = w_type == HQ_GGML_TQ1_0 || w_type == HQ_GGML_TQ1_0_ALT;
+    if (w_type != HQ_GGML_F32 && w_type != HQ_GGML_BF16 && w_type != HQ_GGML_Q8_0 && !tq1)
+        return fail(HQ_ERR_INVALID_ARG, "w_type %d is not F32 (0), Q8_0 (8), BF16 (30) or TQ1_0 (34, 143)", w_type);
+    if (tq1) return hq_tq1_0_gemv(x, w, logits, embedding_dim, vocab_size, stream);
+    if (w_type == HQ_GGML_Q8_0 && embedding_dim % 32)
+        return fail(HQ_ERR_UNSUPPORTED_SHAPE, "Q8_0 needs embedding_dim %% 32 == 0");
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+    if (((uintptr_t)x & 3u) || (w_type == HQ_GGML_F32 && (wa & 3u)) || (w_type != HQ_GGML_Q8_0 && (wa & 1u)))
+        return fail(HQ_ERR_MISALIGNED, "x must be 4-byte aligned, W aligned to its element");
+    int dev = 0;
+    hq_status st = check_device(&dev);
+    if (st != HQ_OK) return st;
+    cudaError_t e = launch_output_projection(x, static_cast<const uint8_t*>(w), w_type, logits, embedding_dim,
+                                             vocab_size, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HQ_OK : cuda_fail(e, "output projection launch");
+}
+
+HQ_API hq_status hq_embedding_lookup(const void* table, int w_type, int token_id, float* out, int embedding_dim,
+                                     int vocab_size, hq_stream_t stream) {
+    if (!table || !out) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (embedding_dim <= 0 || vocab_size <= 0) return fail(HQ_ERR_INVALID_ARG, "bad size");
+    if (token_id < 0 || token_id >= vocab_size)
+        return fail(HQ_ERR_INVALID_ARG, "token_id %d outside [0, %d)", token_id, vocab_size);
+    const bool tq1 = w_type == HQ_GGML_TQ1_0 || w_type == HQ_GGML_TQ1_0_ALT;
+    if (w_type != HQ_GGML_F32 && w_type != HQ_GGML_BF16 && w_type != HQ_GGML_Q8_0 && !tq1)
+        return fail(HQ_ERR_INVALID_ARG, "w_type %d is not F32 (0), Q8_0 (8), BF16 (30) or TQ1_0 (34, 143)", w_type);
+    if ((w_type == HQ_GGML_Q8_0 && embedding_dim % 32) || (tq1 && embedding_dim % 256))
+        return fail(HQ_ERR_UNSUPPORTED_SHAPE, "embedding_dim must hold whole blocks");
+    const uintptr_t ta = reinterpret_cast<uintptr_t>(table);
+    if ((w_type == HQ_GGML_F32 && (ta & 3u)) || (w_type == HQ_GGML_BF16 && (ta & 1u)))
+        return fail(HQ_ERR_MISALIGNED, "table not aligned to its element");
+    int dev = 0;
+    hq_status st = check_device(&dev);
+    if (st != HQ_OK) return st;
+    cudaError_t e = launch_embedding_lookup(static_cast<const uint8_t*>(table), tq1 ? HQ_GGML_TQ1_0 : w_type, token_id,
+                                            out, embedding_dim, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HQ_OK : cuda_fail(e, "embedding lookup launch");
 }
 
 HQ_API void hq_set_launch_overlap(int enable) { set_decode_launch_overlap(enable != 0); }

@@ -1,0 +1,282 @@
+// hq_proj.cu -- the output projection GEMV and the embedding row lookup over
+// the GGML tensor types of the reference's forward pass (gguf_parser.hpp:33-64):
+// F32, BF16, Q8_0 (here) and TQ1_0 (hq_tq1.cu).
+//
+// * proj_dense_kernel<F32 | BF16>: drop-in for the F32 / BF16 branches of
+//   kernel_output_projection (forward_baseline.cu:193-204).  HBM-bound stream:
+//   x staged once per CTA in shared memory, each warp takes 4 rows at a time and
+//   its lanes read 16-byte chunks of all 4 (two chunks per row in flight), so
+//   one shared-memory read of x serves 4 rows.  fp32 FMA per lane, warp sum.
+// * proj_q8_0_kernel: the Q8_0 branch (:205-217).  Q8_0 blocks are 34 bytes
+//   (fp16 d + 32 int8), so a lane takes block pairs (68 bytes, 4-byte aligned)
+//   of 2 rows as 17 words each; int8 -> fp32 is exact with one byte permute
+//   into 2^23 + (q + 128) and one subtract; x is staged with the 16-byte chunks
+//   of each 64-element pair group XOR-swizzled so that the lanes' chunk reads
+//   are bank-conflict free.  Per block sum(q * x) in fp32, then times d.
+// * proj_generic_kernel: any other shape or alignment; one warp per row with
+//   the reference's lane-strided loop.
+// * embedding_kernel: kernel_embedding_lookup (forward_baseline.cu:55-109),
+//   one thread per element.
+#include "hq.h"
+#include "hq_common.cuh"
+#include "hq_internal.h"
+
+namespace hq {
+
+namespace {
+
+constexpr int kProjThreads = 256;
+constexpr int kProjWarps = kProjThreads / 32;
+constexpr int kDenseRows = 4;  // rows per warp, dense kernels
+constexpr int kQ8Rows = 2;     // rows per warp, Q8_0 kernel
+
+enum ProjKind { kF32 = 0, kBF16 = 1 };
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// Stage x (n floats) into shared memory; x 16-byte aligned takes 16-byte loads.
+// swizzle: chunk c (4 floats) of 64-float group p goes to chunk p*16 + ((c%16) ^ (p%16)).
+template <bool kSwizzle>
+__device__ __forceinline__ void stage_x(const float* __restrict__ x, float4* xs4, int n) {
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (int c = threadIdx.x; c < n / 4; c += blockDim.x) {
+            const int dst = kSwizzle ? (c & ~15) | ((c & 15) ^ ((c >> 4) & 15)) : c;
+            xs4[dst] = __ldg(x4 + c);
+        }
+    } else {
+        float* xs = reinterpret_cast<float*>(xs4);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int c = i >> 2;
+            const int dst = kSwizzle ? (c & ~15) | ((c & 15) ^ ((c >> 4) & 15)) : c;
+            xs[dst * 4 + (i & 3)] = __ldg(x + i);
+        }
+    }
+}
+
+template <int kKind>
+__global__ void __launch_bounds__(kProjThreads) proj_dense_kernel(const float* __restrict__ x,
+                                                                  const uint8_t* __restrict__ w,
+                                                                  float* __restrict__ out, int K, int N) {
+    extern __shared__ float4 xs4[];
+    stage_x<false>(x, xs4, K);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t row_bytes = (size_t)K * (kKind == kF32 ? 4 : 2);
+    const int nc = kKind == kF32 ? K / 4 : K / 8;  // 16-byte chunks per row
+    for (int r0 = (blockIdx.x * kProjWarps + warp) * kDenseRows; r0 < N; r0 += gridDim.x * kProjWarps * kDenseRows) {
+        const uint4* p[kDenseRows];
+#pragma unroll
+        for (int i = 0; i < kDenseRows; ++i)
+            p[i] = reinterpret_cast<const uint4*>(w + (size_t)min(r0 + i, N - 1) * row_bytes);
+        float acc[kDenseRows];
+#pragma unroll
+        for (int i = 0; i < kDenseRows; ++i) acc[i] = 0.f;
+#pragma unroll 2
+        for (int c = lane; c < nc; c += 32) {
+            uint4 v[kDenseRows];
+#pragma unroll
+            for (int i = 0; i < kDenseRows; ++i) v[i] = __ldg(p[i] + c);
+            if (kKind == kF32) {
+                const float4 xv = xs4[c];
+#pragma unroll
+                for (int i = 0; i < kDenseRows; ++i) {
+                    acc[i] = fmaf(__uint_as_float(v[i].x), xv.x, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].y), xv.y, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].z), xv.z, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].w), xv.w, acc[i]);
+                }
+            } else {  // bf16: the value's bits are the high half of an fp32 (forward_baseline.cu:200-202)
+                const float4 xa = xs4[2 * c], xb = xs4[2 * c + 1];
+#pragma unroll
+                for (int i = 0; i < kDenseRows; ++i) {
+                    acc[i] = fmaf(__uint_as_float(v[i].x << 16), xa.x, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].x & 0xFFFF0000u), xa.y, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].y << 16), xa.z, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].y & 0xFFFF0000u), xa.w, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].z << 16), xb.x, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].z & 0xFFFF0000u), xb.y, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].w << 16), xb.z, acc[i]);
+                    acc[i] = fmaf(__uint_as_float(v[i].w & 0xFFFF0000u), xb.w, acc[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kDenseRows; ++i) acc[i] = warp_sum(acc[i]);
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < kDenseRows; ++i)
+                if (r0 + i < N) out[r0 + i] = acc[i];
+        }
+    }
+}
+
+// int8 byte `byte` of w (stored as q ^ 0x80 = q + 128) -> exact fp32 q.
+__device__ __forceinline__ float s8x_to_f32(uint32_t wx, uint32_t byte) {
+    return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | byte)) - 8388736.0f;  // 2^23 + 128
+}
+
+__global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __restrict__ x,
+                                                                 const uint8_t* __restrict__ w,
+                                                                 float* __restrict__ out, int K, int N) {
+    extern __shared__ float4 xs4[];
+    stage_x<true>(x, xs4, K);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t row_bytes = (size_t)(K / 32) * 34;
+    const int np = K / 64;  // block pairs per row (68 bytes, 4-byte aligned)
+    for (int r0 = (blockIdx.x * kProjWarps + warp) * kQ8Rows; r0 < N; r0 += gridDim.x * kProjWarps * kQ8Rows) {
+        const uint32_t* p[kQ8Rows];
+#pragma unroll
+        for (int i = 0; i < kQ8Rows; ++i)
+            p[i] = reinterpret_cast<const uint32_t*>(w + (size_t)min(r0 + i, N - 1) * row_bytes);
+        float acc[kQ8Rows];
+#pragma unroll
+        for (int i = 0; i < kQ8Rows; ++i) acc[i] = 0.f;
+        for (int pr = lane; pr < np; pr += 32) {
+            uint32_t W[kQ8Rows][17];
+#pragma unroll
+            for (int i = 0; i < kQ8Rows; ++i)
+#pragma unroll
+                for (int k = 0; k < 17; ++k) W[i][k] = __ldg(p[i] + pr * 17 + k);
+            const float4* xg = xs4 + pr * 16;
+            const int sw = pr & 15;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                float s[kQ8Rows];
+#pragma unroll
+                for (int i = 0; i < kQ8Rows; ++i) s[i] = 0.f;
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {  // elements 4 q4 .. 4 q4 + 3 of the block
+                    const float4 xv = xg[(blk * 8 + q4) ^ sw];
+                    const float xe[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int off = blk * 34 + 2 + 4 * q4 + e;  // byte offset in the pair
+#pragma unroll
+                        for (int i = 0; i < kQ8Rows; ++i)
+                            s[i] = fmaf(s8x_to_f32(W[i][off >> 2] ^ 0x80808080u, (uint32_t)(off & 3)), xe[e], s[i]);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kQ8Rows; ++i) {
+                    const uint32_t dbits = blk == 0 ? (W[i][0] & 0xFFFFu) : (W[i][8] >> 16);
+                    acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)dbits)), s[i], acc[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kQ8Rows; ++i) acc[i] = warp_sum(acc[i]);
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < kQ8Rows; ++i)
+                if (r0 + i < N) out[r0 + i] = acc[i];
+        }
+    }
+}
+
+// The reference's loop (forward_baseline.cu:193-217) for shapes and alignments
+// the stream kernels do not take; x read from global memory.
+__global__ void __launch_bounds__(kProjThreads) proj_generic_kernel(const float* __restrict__ x,
+                                                                    const uint8_t* __restrict__ w, int type,
+                                                                    float* __restrict__ out, int K, int N) {
+    const int lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * kProjWarps + (threadIdx.x >> 5); row < N; row += gridDim.x * kProjWarps) {
+        float acc = 0.f;
+        if (type == HQ_GGML_F32) {
+            const float* r = reinterpret_cast<const float*>(w) + (size_t)row * K;
+            for (int i = lane; i < K; i += 32) acc = fmaf(r[i], x[i], acc);
+        } else if (type == HQ_GGML_BF16) {
+            const uint16_t* r = reinterpret_cast<const uint16_t*>(w) + (size_t)row * K;
+            for (int i = lane; i < K; i += 32) acc = fmaf(__uint_as_float((uint32_t)r[i] << 16), x[i], acc);
+        } else {  // Q8_0
+            const int nb = K / 32;
+            const uint8_t* r = w + (size_t)row * nb * 34;
+            for (int b = lane; b < nb; b += 32) {
+                const uint8_t* blk = r + (size_t)b * 34;
+                const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+                for (int j = 0; j < 32; ++j) acc = fmaf(d * (float)(int8_t)blk[2 + j], x[b * 32 + j], acc);
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) out[row] = acc;
+    }
+}
+
+__global__ void embedding_kernel(const uint8_t* __restrict__ table, int type, int token_id, float* __restrict__ out,
+                                 int K) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= K) return;
+    if (type == HQ_GGML_F32) {
+        out[i] = reinterpret_cast<const float*>(table)[(size_t)token_id * K + i];
+    } else if (type == HQ_GGML_BF16) {
+        out[i] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(table)[(size_t)token_id * K + i] << 16);
+    } else if (type == HQ_GGML_Q8_0) {
+        const uint8_t* blk = table + ((size_t)token_id * (K / 32) + i / 32) * 34;
+        const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        out[i] = d * (float)(int8_t)blk[2 + i % 32];
+    } else {  // TQ1_0 (native_decoder.cu:63-103): NaN/Inf d -> 0
+        const uint8_t* blk = table + ((size_t)token_id * (K / 256) + i / 256) * 56;
+        float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        if (isnan(d) || isinf(d)) d = 0.f;
+        const int e = i % 256;
+        uint32_t v = e < 250 ? blk[2 + e / 5] : blk[52 + (e - 250) / 3];
+        const int s = e < 250 ? e % 5 : (e - 250) % 3;
+        for (int k = 0; k < s; ++k) v /= 3u;
+        out[i] = d * (float)((int)(v % 3u) - 1);
+    }
+}
+
+cudaError_t launch_stream_kernel(const void* fn, const float* x, const uint8_t* w, float* out, int K, int N,
+                                 int rows_per_warp, size_t smem, cudaStream_t s) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = ensure_smem_attr(fn, dev, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kProjThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const int want = (N + kProjWarps * rows_per_warp - 1) / (kProjWarps * rows_per_warp);
+    const int cap = device_info(dev).sm_count * per_sm;
+    const int grid = want < cap ? want : cap;
+    void* args[] = {(void*)&x, (void*)&w, (void*)&out, (void*)&K, (void*)&N};
+    return cudaLaunchKernel(fn, grid, kProjThreads, args, smem, s);
+}
+
+}  // namespace
+
+cudaError_t launch_output_projection(const float* x, const uint8_t* w, int type, float* out, int K, int N,
+                                     cudaStream_t s) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = (size_t)K * sizeof(float);
+    const bool x_fits = smem + 4096 <= device_info(dev).smem_optin;
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+    if (type == HQ_GGML_F32 && x_fits && K % 4 == 0 && (wa & 15u) == 0)
+        return launch_stream_kernel(reinterpret_cast<const void*>(proj_dense_kernel<kF32>), x, w, out, K, N,
+                                    kDenseRows, smem, s);
+    if (type == HQ_GGML_BF16 && x_fits && K % 8 == 0 && (wa & 15u) == 0)
+        return launch_stream_kernel(reinterpret_cast<const void*>(proj_dense_kernel<kBF16>), x, w, out, K, N,
+                                    kDenseRows, smem, s);
+    if (type == HQ_GGML_Q8_0 && x_fits && K % 64 == 0 && (wa & 3u) == 0)
+        return launch_stream_kernel(reinterpret_cast<const void*>(proj_q8_0_kernel), x, w, out, K, N, kQ8Rows,
+                                    smem, s);
+    const int blocks = (N + kProjWarps - 1) / kProjWarps;
+    const int grid = blocks < device_info(dev).sm_count * 16 ? blocks : device_info(dev).sm_count * 16;
+    proj_generic_kernel<<<grid, kProjThreads, 0, s>>>(x, w, type, out, K, N);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embedding_lookup(const uint8_t* table, int type, int token_id, float* out, int K, cudaStream_t s) {
+    embedding_kernel<<<(K + 255) / 256, 256, 0, s>>>(table, type, token_id, out, K);
+    return cudaGetLastError();
+}
+
+}  // namespace hq

@@ -22,7 +22,8 @@ from ._lib import (HQ_BF16, HQ_F16, HQ_F32, HQ_WFMT_LINEAR_T2, HQ_WFMT_LINEAR_U4
                    HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TQ1_0, HQError, check, lib)
 
 __all__ = ["HQError", "weight_bytes", "repack_host", "repack", "make_workspace", "gemm", "QuantLinear",
-           "tq1_0_gemv", "tq1_0_to_tile_t2", "check_device_error", "MarlinGemmEngine",
+           "tq1_0_gemv", "tq1_0_to_tile_t2", "output_projection", "embedding_lookup", "check_device_error",
+           "MarlinGemmEngine",
            "HQ_WFMT_LINEAR_U4", "HQ_WFMT_MARLIN_QUAD", "HQ_WFMT_TILE_U4", "HQ_WFMT_LINEAR_T2",
            "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0"]
 
@@ -121,6 +122,28 @@ def tq1_0_gemv(x: torch.Tensor, w: torch.Tensor, out_dim: int, out: torch.Tensor
     if out is None:
         out = torch.empty(out_dim, dtype=torch.float32, device=x.device)
     check(lib().hq_tq1_0_gemv(_ptr(x), _ptr(w), _ptr(out), in_dim, out_dim, _stream(stream)))
+    return out
+
+
+def output_projection(x: torch.Tensor, w: torch.Tensor, w_type: int, vocab_size: int,
+                      out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """kernel_output_projection (forward_baseline.cu:178-257): logits = W x over GGML F32 / BF16 / Q8_0 /
+    TQ1_0 rows (w_type: _lib.HQ_GGML_*), fp32 x and logits."""
+    embedding_dim = x.numel()
+    if out is None:
+        out = torch.empty(vocab_size, dtype=torch.float32, device=x.device)
+    check(lib().hq_output_projection(_ptr(x), _ptr(w), w_type, _ptr(out), embedding_dim, vocab_size,
+                                     _stream(stream)))
+    return out
+
+
+def embedding_lookup(table: torch.Tensor, w_type: int, token_id: int, embedding_dim: int, vocab_size: int,
+                     out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """kernel_embedding_lookup (forward_baseline.cu:55-109): row token_id of a GGML table as fp32."""
+    if out is None:
+        out = torch.empty(embedding_dim, dtype=torch.float32, device=table.device)
+    check(lib().hq_embedding_lookup(_ptr(table), w_type, token_id, _ptr(out), embedding_dim, vocab_size,
+                                    _stream(stream)))
     return out
 
 

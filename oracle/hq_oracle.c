@@ -459,3 +459,119 @@ int hqo_gemv_tq1_0(const float* x, const uint8_t* w, float* out, int in_dim,
     }
     return 0;
 }
+
+/* ------------------------------------------------- output / embedding */
+
+static void warp_tree(float lanes[32]) {  /* forward_baseline.cu:42-48 */
+    for (int off = 16; off > 0; off /= 2) {
+        float nxt[32];
+        for (int i = 0; i < 32; ++i) nxt[i] = lanes[i] + (i + off < 32 ? lanes[i + off] : lanes[i]);
+        memcpy(lanes, nxt, 32 * sizeof(float));
+    }
+}
+
+static int tq1_trit(const uint8_t* blk, int e) {  /* element e of a TQ1_0 block, native_decoder.cu:81-101 */
+    uint32_t val;
+    int s;
+    if (e < 250) {
+        val = blk[2 + e / 5];
+        s = e % 5;
+    } else {
+        val = blk[2 + 50 + (e - 250) / 3];
+        s = (e - 250) % 3;
+    }
+    for (int i = 0; i < s; ++i) val /= 3;
+    return (int)(val % 3) - 1;
+}
+
+int hqo_output_projection(const float* x, const void* w, int type, float* logits,
+                          int embedding_dim, int vocab_size, int nthreads) {
+    const int K = embedding_dim;
+    if (!x || !w || !logits || K <= 0 || vocab_size <= 0) return HQO_EINVAL;
+    const int tq1 = type == HQO_GGML_TQ1_0 || type == HQO_GGML_TQ1_0_ALT;
+    if (type != HQO_GGML_F32 && type != HQO_GGML_BF16 && type != HQO_GGML_Q8_0 && !tq1) return HQO_EINVAL;
+    if ((type == HQO_GGML_Q8_0 && K % 32) || (tq1 && K % 256)) return HQO_EINVAL;
+    nthreads = set_threads(nthreads);
+    #pragma omp parallel for num_threads(nthreads) schedule(static)
+    for (int row = 0; row < vocab_size; ++row) {
+        float lanes[32];
+        for (int lane = 0; lane < 32; ++lane) {
+            float acc = 0.0f;
+            if (type == HQO_GGML_F32) {
+                const float* r = (const float*)w + (size_t)row * K;
+                for (int i = lane; i < K; i += 32) acc = fmaf(r[i], x[i], acc);
+            } else if (type == HQO_GGML_BF16) {
+                const uint16_t* r = (const uint16_t*)w + (size_t)row * K;
+                for (int i = lane; i < K; i += 32) {
+                    const uint32_t u = (uint32_t)r[i] << 16;
+                    float f;
+                    memcpy(&f, &u, 4);
+                    acc = fmaf(f, x[i], acc);
+                }
+            } else if (type == HQO_GGML_Q8_0) {
+                const int nb = K / 32;
+                const uint8_t* r = (const uint8_t*)w + (size_t)row * nb * 34;
+                for (int b = lane; b < nb; b += 32) {
+                    const uint8_t* blk = r + (size_t)b * 34;
+                    const float d = hqo_half_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+                    for (int j = 0; j < 32; ++j) acc = fmaf(d * (float)(int8_t)blk[2 + j], x[b * 32 + j], acc);
+                }
+            } else {
+                const int nb = K / 256;
+                const uint8_t* r = (const uint8_t*)w + (size_t)row * nb * 56;
+                for (int b = 0; b < nb; ++b) {
+                    const uint8_t* blk = r + (size_t)b * 56;
+                    float d = hqo_half_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+                    if (isnan(d) || isinf(d)) d = 0.0f;
+                    for (int by = lane; by < 50; by += 32) {
+                        uint32_t val = blk[2 + by];
+                        for (int t = 0; t < 5; ++t) {
+                            const int trit = (int)(val % 3) - 1;
+                            val /= 3;
+                            acc = fmaf(d * (float)trit, x[b * 256 + by * 5 + t], acc);
+                        }
+                    }
+                    if (lane < 2) {
+                        uint32_t val = blk[2 + 50 + lane];
+                        for (int t = 0; t < 3; ++t) {
+                            const int trit = (int)(val % 3) - 1;
+                            val /= 3;
+                            acc = fmaf(d * (float)trit, x[b * 256 + 250 + lane * 3 + t], acc);
+                        }
+                    }
+                }
+            }
+            lanes[lane] = acc;
+        }
+        warp_tree(lanes);
+        logits[row] = lanes[0];
+    }
+    return 0;
+}
+
+int hqo_embedding_lookup(const void* table, int type, int token_id, float* out, int embedding_dim) {
+    const int K = embedding_dim;
+    if (!table || !out || K <= 0 || token_id < 0) return HQO_EINVAL;
+    const int tq1 = type == HQO_GGML_TQ1_0 || type == HQO_GGML_TQ1_0_ALT;
+    if ((type == HQO_GGML_Q8_0 && K % 32) || (tq1 && K % 256)) return HQO_EINVAL;
+    for (int i = 0; i < K; ++i) {
+        if (type == HQO_GGML_F32) {
+            out[i] = ((const float*)table)[(size_t)token_id * K + i];
+        } else if (type == HQO_GGML_BF16) {
+            const uint32_t u = (uint32_t)((const uint16_t*)table)[(size_t)token_id * K + i] << 16;
+            memcpy(&out[i], &u, 4);
+        } else if (type == HQO_GGML_Q8_0) {
+            const uint8_t* blk = (const uint8_t*)table + ((size_t)token_id * (K / 32) + i / 32) * 34;
+            const float d = hqo_half_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+            out[i] = d * (float)(int8_t)blk[2 + i % 32];
+        } else if (tq1) {
+            const uint8_t* blk = (const uint8_t*)table + ((size_t)token_id * (K / 256) + i / 256) * 56;
+            float d = hqo_half_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+            if (isnan(d) || isinf(d)) d = 0.0f;
+            out[i] = d * (float)tq1_trit(blk, i % 256);
+        } else {
+            return HQO_EINVAL;
+        }
+    }
+    return 0;
+}

@@ -89,6 +89,31 @@ int hqo_t2_gemm(const float* X, const uint32_t* linear_t2, const float* scales,
 int hqo_gemv_tq1_0(const float* x, const uint8_t* w, float* out, int in_dim,
                    int out_dim, int nthreads);
 
+/* GGML tensor types taken by the projection routines (gguf_parser.hpp:33-64). */
+#define HQO_GGML_F32 0
+#define HQO_GGML_Q8_0 8
+#define HQO_GGML_BF16 30
+#define HQO_GGML_TQ1_0 34
+#define HQO_GGML_TQ1_0_ALT 143 /* also read as TQ1_0 (forward_baseline.cu:82,218) */
+
+/* kernel_output_projection (forward_baseline.cu:178-257): logits[row] =
+ * dot(W[row, :], x), one warp per row.  Restated with its 32 lane partial sums
+ * (F32 / BF16: elements lane + 32 i; Q8_0: blocks lane + 32 i, element order
+ * within a block; TQ1_0: every block, packed bytes lane and lane + 32 below 50,
+ * lanes 0-1 bytes 50-51), its fp32 arithmetic with the multiply-adds fused the
+ * way nvcc contracts them, and the shuffle-down tree (:42-48).  Q8_0 applies d
+ * unchecked; TQ1_0 replaces a NaN/Inf d by 0 (:223).  W rows: F32 / BF16
+ * embedding_dim elements, Q8_0 embedding_dim/32 blocks of 34 bytes, TQ1_0
+ * embedding_dim/256 blocks of 56 bytes. */
+int hqo_output_projection(const float* x, const void* w, int type, float* logits,
+                          int embedding_dim, int vocab_size, int nthreads);
+
+/* kernel_embedding_lookup (forward_baseline.cu:55-109): row token_id of the
+ * table, dequantised to fp32 (Q8_0: d * q; TQ1_0: d * trit with a NaN/Inf d
+ * replaced by 0, as native_decoder.cu:63-103). */
+int hqo_embedding_lookup(const void* table, int type, int token_id, float* out,
+                         int embedding_dim);
+
 #ifdef __cplusplus
 }
 #endif

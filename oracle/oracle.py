@@ -242,6 +242,37 @@ def gemv_tq1_0(x, blob, in_dim, out_dim, nthreads=0):
     return out
 
 
+GGML_F32, GGML_Q8_0, GGML_BF16, GGML_TQ1_0 = 0, 8, 30, 34  # gguf_parser.hpp:33-64
+
+
+def output_projection(x, w, w_type, embedding_dim, vocab_size, nthreads=0):
+    """kernel_output_projection (forward_baseline.cu:178-257) restated: logits = W x."""
+    out = np.empty(vocab_size, np.float32)
+    wa = np.ascontiguousarray(w)
+    _ck(lib().hqo_output_projection(_p(np.ascontiguousarray(x, np.float32)), _p(wa), w_type, _p(out),
+                                    embedding_dim, vocab_size, nthreads), "output_projection")
+    return out
+
+
+def embedding_lookup(table, w_type, token_id, embedding_dim):
+    """kernel_embedding_lookup (forward_baseline.cu:55-109) restated: row token_id as fp32."""
+    out = np.empty(embedding_dim, np.float32)
+    _ck(lib().hqo_embedding_lookup(_p(np.ascontiguousarray(table)), w_type, token_id, _p(out), embedding_dim),
+        "embedding_lookup")
+    return out
+
+
+def pack_q8_0(q, d_bits):
+    """Q8_0 blocks (forward_baseline.cu:30-33): per 32 weights fp16 d (bits) + 32 int8, 34 bytes.
+    q int8 [N][K], d_bits uint16 [N][K/32] -> uint8 [N * K/32 * 34]."""
+    q = np.asarray(q, np.int8)
+    N, K = q.shape
+    blk = np.empty((N, K // 32, 34), np.uint8)
+    blk[:, :, 0:2] = np.asarray(d_bits, np.uint16).reshape(N, K // 32, 1).view(np.uint8)
+    blk[:, :, 2:] = q.reshape(N, K // 32, 32).view(np.uint8)
+    return blk.ravel()
+
+
 def max_rel_err(y, y_ref) -> float:
     """max|y - y_ref| / max|y_ref| over the whole output tensor."""
     y = np.asarray(y, np.float64)

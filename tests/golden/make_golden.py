@@ -76,6 +76,31 @@ def tq1_case(prefix, K, N, seed, out):
                 f"{prefix}_meta": np.array([K, N, seed], np.int64)})
 
 
+def proj_case(prefix, w_type, K, N, seed, out):
+    """Output projection and embedding rows (forward_baseline.cu:55-109, 178-257) over a GGML type."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = rng.standard_normal(K, dtype=np.float32)
+    if w_type == o.GGML_F32:
+        w = rng.standard_normal((N, K), dtype=np.float32).view(np.uint8).ravel()
+    elif w_type == o.GGML_BF16:
+        w = (rng.standard_normal((N, K), dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).ravel()
+    elif w_type == o.GGML_Q8_0:
+        q = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+        d = rng.uniform(0.005, 0.02, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+        d[2, 1] = 0x7E00  # NaN d: applied unchecked, the row's logit is NaN as in the reference
+        w = o.pack_q8_0(q, d)
+    else:
+        t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+        d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+        d[1, 0] = 0x7C00  # Inf d: read as 0 (forward_baseline.cu:223)
+        w = o.pack_tq1_0(t, d)
+    y = o.output_projection(x, w, w_type, K, N, nthreads=1)
+    tokens = np.array([0, N // 2, N - 1], np.int64)
+    emb = np.stack([o.embedding_lookup(w, w_type, int(tk), K) for tk in tokens])
+    out.update({f"{prefix}_x": x, f"{prefix}_w": w, f"{prefix}_y": y, f"{prefix}_tokens": tokens,
+                f"{prefix}_emb": emb, f"{prefix}_meta": np.array([w_type, K, N, seed], np.int64)})
+
+
 def main():
     out: dict[str, np.ndarray] = {}
     int4_case("i4a", 3, 256, 48, 128, 7, "f16", out)       # N=48: one ragged strip group
@@ -84,6 +109,10 @@ def main():
     t2_case("t2a", 2, 256, 32, 128, 17, "f16", out)
     t2_case("t2b", 9, 512, 144, 128, 19, "bf16", out)
     tq1_case("tq1", 768, 40, 23, out)
+    proj_case("pf32", o.GGML_F32, 200, 37, 29, out)     # K % 8 != 0
+    proj_case("pbf16", o.GGML_BF16, 264, 37, 31, out)
+    proj_case("pq8", o.GGML_Q8_0, 320, 37, 37, out)      # one NaN block scale
+    proj_case("ptq1", 143, 512, 21, 41, out)             # TQ1_0 under its alternate type id; one Inf d
     # BASELINE config 0, full size: store checksums of the inputs and the output.
     A, q, S = o.gen_int4_case(16, 4096, 4096, group=128, seed=0, a_dtype="f16")
     lin = o.pack_linear_u4(q)

@@ -134,3 +134,19 @@ def test_tq1_gemv_argument_errors():
     p = ctypes.c_void_p(buf.ctypes.data + (-buf.ctypes.data) % 16)
     assert L.hq_tq1_0_gemv(None, p, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG
     assert L.hq_tq1_0_gemv(p, p, p, 200, 4, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+
+
+def test_projection_argument_errors():
+    L = _lib.lib()
+    buf = np.zeros(4096, np.uint8)
+    p = ctypes.c_void_p(buf.ctypes.data + (-buf.ctypes.data) % 16)
+    odd = ctypes.c_void_p(p.value + 1)
+    assert L.hq_output_projection(None, p, _lib.HQ_GGML_BF16, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG
+    assert L.hq_output_projection(p, p, 12, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG  # Q4_K: not a projection type
+    assert L.hq_output_projection(p, p, _lib.HQ_GGML_Q8_0, p, 48, 4, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert L.hq_output_projection(p, p, _lib.HQ_GGML_TQ1_0_ALT, p, 200, 4, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert L.hq_output_projection(p, odd, _lib.HQ_GGML_BF16, p, 256, 4, None) == _lib.HQ_ERR_MISALIGNED
+    assert L.hq_embedding_lookup(p, _lib.HQ_GGML_F32, 4, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG  # token >= vocab
+    assert L.hq_embedding_lookup(p, _lib.HQ_GGML_F32, -1, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG
+    assert L.hq_embedding_lookup(p, _lib.HQ_GGML_Q8_0, 0, p, 40, 4, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert L.hq_embedding_lookup(p, 2, 0, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG

@@ -78,6 +78,44 @@ def test_golden_tq1(golden):
     assert np.array_equal(o.gemv_tq1_0(golden["tq1_x"], blob, K, N), golden["tq1_y"])
 
 
+@pytest.mark.parametrize("prefix", ["pf32", "pbf16", "pq8", "ptq1"])
+def test_golden_projection(golden, prefix):
+    w_type, K, N, _ = (int(v) for v in golden[f"{prefix}_meta"])
+    w = golden[f"{prefix}_w"]
+    y = o.output_projection(golden[f"{prefix}_x"], w, w_type, K, N)
+    assert np.array_equal(y, golden[f"{prefix}_y"], equal_nan=True)
+    for tk, row in zip(golden[f"{prefix}_tokens"], golden[f"{prefix}_emb"]):
+        assert np.array_equal(o.embedding_lookup(w, w_type, int(tk), K), row)
+
+
+def test_projection_restatement_against_float64():
+    """The restated projection against an independent float64 dot product of the decoded weights."""
+    rng = np.random.default_rng(3)
+    K, N = 320, 9
+    x = rng.standard_normal(K).astype(np.float32)
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    assert o.max_rel_err(o.output_projection(x, W, o.GGML_F32, K, N), W.astype(np.float64) @ x) < 1e-6
+    bf = (W.view(np.uint32) >> 16).astype(np.uint16)
+    Wb = (bf.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    assert o.max_rel_err(o.output_projection(x, bf, o.GGML_BF16, K, N), Wb @ x) < 1e-6
+    q = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.02, (N, K // 32)).astype(np.float16)
+    blob = o.pack_q8_0(q, d.view(np.uint16))
+    Wq = (q.reshape(N, K // 32, 32) * d.astype(np.float64)[:, :, None]).reshape(N, K)
+    assert o.max_rel_err(o.output_projection(x, blob, o.GGML_Q8_0, K, N), Wq @ x) < 1e-6
+    for tk in (0, N - 1):
+        assert np.array_equal(o.embedding_lookup(blob, o.GGML_Q8_0, tk, K), Wq[tk].astype(np.float32))
+    # TQ1_0: the projection's restatement and the decoder GEMV's agree where every d is finite
+    t = rng.integers(-1, 2, (N, 512), dtype=np.int8)
+    dt = rng.uniform(0.01, 0.05, (N, 2)).astype(np.float16).view(np.uint16)
+    tb = o.pack_tq1_0(t, dt)
+    x2 = rng.standard_normal(512).astype(np.float32)
+    assert o.max_rel_err(o.output_projection(x2, tb, o.GGML_TQ1_0, 512, N), o.gemv_tq1_0(x2, tb, 512, N)) < 1e-6
+    emb = o.embedding_lookup(tb, o.GGML_TQ1_0, 4, 512)
+    dd = dt[4].view(np.float16).astype(np.float32)
+    assert np.array_equal(emb, (t[4].reshape(2, 256) * dd[:, None]).ravel().astype(np.float32))
+
+
 def test_golden_config0_checksums(golden):
     import hashlib
     A, q, S = o.gen_int4_case(16, 4096, 4096, group=128, seed=0, a_dtype="f16")
