@@ -495,6 +495,25 @@ def run_case(args):
     from nebula_b200 import _lib, hq
     f = args.case.split(",")
     dev = torch.device("cuda", 0)
+    if f[0] == "proj":  # proj,TYPE,K,N: hq_output_projection over GGML TYPE (0 F32, 8 Q8_0, 30 BF16) rows
+        w_type, K, N = int(f[1]), int(f[2]), int(f[3])
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        if w_type == _lib.HQ_GGML_Q8_0:
+            W = torch.randint(-128, 128, (N, K // 32, 34), dtype=torch.int8, device=dev, generator=g).view(torch.uint8)
+            W[..., 0:2] = (torch.rand((N, K // 32), device=dev, generator=g) * 0.015 + 0.005).half().view(
+                torch.uint8).view(N, K // 32, 2)
+        elif w_type == _lib.HQ_GGML_BF16:
+            W = torch.randn((N, K), device=dev, generator=g).bfloat16().view(torch.uint8)
+        else:
+            W = torch.randn((N, K), device=dev, generator=g).view(torch.uint8)
+        x = torch.randn(K, device=dev, generator=g)
+        for _ in range(args.steps):
+            y = hq.output_projection(x, W.reshape(-1), w_type, N)
+        torch.cuda.synchronize()
+        hq.check_device_error()
+        print(json.dumps({"case": args.case, "checksum": float(y.abs().sum())}))
+        return 0
     if f[0] == "tq1":  # tq1,K,N: hq_tq1_0_gemv on well-formed TQ1_0 blocks (packed 0..242, d ~ U(0.01, 0.05))
         K, N = int(f[1]), int(f[2])
         g = torch.Generator(device=dev)
@@ -542,7 +561,7 @@ def main():
     ap.add_argument("--no-stack", action="store_true", help="skip the TP layer stack (configs[4])")
     ap.add_argument("--case", default=None,
                     help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits; "
-                         "'tq1,K,N' runs hq_tq1_0_gemv instead")
+                         "'tq1,K,N' runs hq_tq1_0_gemv, 'proj,TYPE,K,N' hq_output_projection instead")
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")

@@ -8,11 +8,14 @@
 //   its lanes read 16-byte chunks of all 4 (two chunks per row in flight), so
 //   one shared-memory read of x serves 4 rows.  fp32 FMA per lane, warp sum.
 // * proj_q8_0_kernel: the Q8_0 branch (:205-217).  Q8_0 blocks are 34 bytes
-//   (fp16 d + 32 int8), so a lane takes block pairs (68 bytes, 4-byte aligned)
-//   of 2 rows as 17 words each; int8 -> fp32 is exact with one byte permute
-//   into 2^23 + (q + 128) and one subtract; x is staged with the 16-byte chunks
-//   of each 64-element pair group XOR-swizzled so that the lanes' chunk reads
-//   are bank-conflict free.  Per block sum(q * x) in fp32, then times d.
+//   (fp16 d + 32 int8): each warp copies 32 block pairs (2176 contiguous,
+//   16-byte aligned bytes) of 2 rows into its two-stage shared-memory buffer
+//   with 16-byte cp.async, one step ahead; then each lane takes one pair
+//   (68 bytes, 17 words: a word stride of 17 is bank-conflict free).  int8 ->
+//   fp32 is exact with one byte permute into 2^23 + (q + 128) and one subtract;
+//   x is staged with the 16-byte chunks of each 64-element pair group
+//   XOR-swizzled so that the lanes' chunk reads are bank-conflict free.  Per
+//   block sum(q * x) in fp32, then times d.
 // * proj_generic_kernel: any other shape or alignment; one warp per row with
 //   the reference's lane-strided loop.
 // * embedding_kernel: kernel_embedding_lookup (forward_baseline.cu:55-109),
@@ -120,36 +123,83 @@ __device__ __forceinline__ float s8x_to_f32(uint32_t wx, uint32_t byte) {
     return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | byte)) - 8388736.0f;  // 2^23 + 128
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+constexpr int kQ8PairsPerStep = 32;                 // one block pair per lane
+constexpr int kQ8StepBytes = kQ8PairsPerStep * 68;  // 2176 B of one row
+constexpr int kQ8StageBytes = kQ8Rows * kQ8StepBytes;
+
+// x (K floats, swizzled) then per warp two stages of kQ8Rows x 2176 bytes.
+__host__ __device__ inline size_t q8_smem_bytes(int K) {
+    return (size_t)K * sizeof(float) + (size_t)kProjWarps * 2 * kQ8StageBytes;
+}
+
 __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __restrict__ x,
                                                                  const uint8_t* __restrict__ w,
                                                                  float* __restrict__ out, int K, int N) {
     extern __shared__ float4 xs4[];
     stage_x<true>(x, xs4, K);
-    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t row_bytes = (size_t)(K / 32) * 34;
-    const int np = K / 64;  // block pairs per row (68 bytes, 4-byte aligned)
-    for (int r0 = (blockIdx.x * kProjWarps + warp) * kQ8Rows; r0 < N; r0 += gridDim.x * kProjWarps * kQ8Rows) {
-        const uint32_t* p[kQ8Rows];
+    const uint32_t stage0 = smem_u32(reinterpret_cast<uint8_t*>(xs4) + (size_t)K * sizeof(float) +
+                                     (size_t)warp * 2 * kQ8StageBytes);
+    const size_t row_bytes = (size_t)(K / 32) * 34;  // a multiple of 16 (K % 256 == 0)
+    const int np = K / 64;                            // block pairs per row
+    const int nj = (np + kQ8PairsPerStep - 1) / kQ8PairsPerStep;
+    const int first = blockIdx.x * kProjWarps + warp, stride = gridDim.x * kProjWarps;  // row pairs
+    const int n_rp = (N + kQ8Rows - 1) / kQ8Rows;
+    const int my_rp = first < n_rp ? (n_rp - first + stride - 1) / stride : 0;
+    const int n_steps = my_rp * nj;
+
+    // step s: row pair first + (s / nj) * stride, pairs [32 (s % nj), +32) of both rows, into stage s & 1
+    auto issue = [&](int st) {
+        if (st < n_steps) {
+            const int rp = first + (st / nj) * stride, j = st % nj;
+            const int pairs = min(kQ8PairsPerStep, np - j * kQ8PairsPerStep);
+            const int chunks = pairs * 68 / 16;  // pairs % 4 == 0
 #pragma unroll
-        for (int i = 0; i < kQ8Rows; ++i)
-            p[i] = reinterpret_cast<const uint32_t*>(w + (size_t)min(r0 + i, N - 1) * row_bytes);
-        float acc[kQ8Rows];
+            for (int i = 0; i < kQ8Rows; ++i) {
+                const uint8_t* src = w + (size_t)min(rp * kQ8Rows + i, N - 1) * row_bytes + (size_t)j * kQ8StepBytes;
+                const uint32_t dst = stage0 + (st & 1) * kQ8StageBytes + i * kQ8StepBytes;
+                for (int c = lane; c < chunks; c += 32) cp_async16(dst + 16 * c, src + 16 * c);
+            }
+        }
+        cp_async_commit();  // one group per step, empty past the end
+    };
+    issue(0);
+    issue(1);
+    __syncthreads();  // x staged
+
+    float acc[kQ8Rows];
 #pragma unroll
-        for (int i = 0; i < kQ8Rows; ++i) acc[i] = 0.f;
-        for (int pr = lane; pr < np; pr += 32) {
+    for (int i = 0; i < kQ8Rows; ++i) acc[i] = 0.f;
+    for (int st = 0; st < n_steps; ++st) {
+        const int rp = first + (st / nj) * stride, j = st % nj;
+        cp_async_wait_1();  // this lane's copies of step st are done
+        __syncwarp();       // ... and every lane's
+        const int pr = j * kQ8PairsPerStep + lane;
+        if (pr < np) {
+            const uint32_t sp = stage0 + (st & 1) * kQ8StageBytes + lane * 68;  // word stride 17: no bank conflicts
             uint32_t W[kQ8Rows][17];
 #pragma unroll
             for (int i = 0; i < kQ8Rows; ++i)
 #pragma unroll
-                for (int k = 0; k < 17; ++k) W[i][k] = __ldg(p[i] + pr * 17 + k);
+                for (int k = 0; k < 17; ++k)
+                    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(W[i][k]) : "r"(sp + i * kQ8StepBytes + 4 * k));
             const float4* xg = xs4 + pr * 16;
             const int sw = pr & 15;
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-                float s[kQ8Rows];
+            for (int i = 0; i < kQ8Rows; ++i)
 #pragma unroll
-                for (int i = 0; i < kQ8Rows; ++i) s[i] = 0.f;
+                for (int k = 0; k < 17; ++k) W[i][k] ^= 0x80808080u;  // q + 128 per byte
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                float s[kQ8Rows][2];  // two chains per row: even / odd elements
+#pragma unroll
+                for (int i = 0; i < kQ8Rows; ++i) s[i][0] = s[i][1] = 0.f;
 #pragma unroll
                 for (int q4 = 0; q4 < 8; ++q4) {  // elements 4 q4 .. 4 q4 + 3 of the block
                     const float4 xv = xg[(blk * 8 + q4) ^ sw];
@@ -159,24 +209,29 @@ __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __
                         const int off = blk * 34 + 2 + 4 * q4 + e;  // byte offset in the pair
 #pragma unroll
                         for (int i = 0; i < kQ8Rows; ++i)
-                            s[i] = fmaf(s8x_to_f32(W[i][off >> 2] ^ 0x80808080u, (uint32_t)(off & 3)), xe[e], s[i]);
+                            s[i][e & 1] = fmaf(s8x_to_f32(W[i][off >> 2], (uint32_t)(off & 3)), xe[e], s[i][e & 1]);
                     }
                 }
 #pragma unroll
                 for (int i = 0; i < kQ8Rows; ++i) {
-                    const uint32_t dbits = blk == 0 ? (W[i][0] & 0xFFFFu) : (W[i][8] >> 16);
-                    acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)dbits)), s[i], acc[i]);
+                    // d sits in the pair's bytes 0-1 (block 0) and 34-35 (block 1); undo the ^ 0x80 above
+                    const uint32_t dbits = (blk == 0 ? (W[i][0] & 0xFFFFu) : (W[i][8] >> 16)) ^ 0x8080u;
+                    acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)dbits)), s[i][0] + s[i][1], acc[i]);
                 }
             }
         }
+        __syncwarp();  // every lane is done with stage st & 1
+        issue(st + 2);
+        if (j == nj - 1) {  // row pair done
 #pragma unroll
-        for (int i = 0; i < kQ8Rows; ++i) acc[i] = warp_sum(acc[i]);
-        if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < kQ8Rows; ++i)
-                if (r0 + i < N) out[r0 + i] = acc[i];
+            for (int i = 0; i < kQ8Rows; ++i) {
+                const float v = warp_sum(acc[i]);
+                if (lane == 0 && rp * kQ8Rows + i < N) out[rp * kQ8Rows + i] = v;
+                acc[i] = 0.f;
+            }
         }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // The reference's loop (forward_baseline.cu:193-217) for shapes and alignments
@@ -265,9 +320,10 @@ cudaError_t launch_output_projection(const float* x, const uint8_t* w, int type,
     if (type == HQ_GGML_BF16 && x_fits && K % 8 == 0 && (wa & 15u) == 0)
         return launch_stream_kernel(reinterpret_cast<const void*>(proj_dense_kernel<kBF16>), x, w, out, K, N,
                                     kDenseRows, smem, s);
-    if (type == HQ_GGML_Q8_0 && x_fits && K % 64 == 0 && (wa & 3u) == 0)
+    if (type == HQ_GGML_Q8_0 && q8_smem_bytes(K) + 4096 <= device_info(dev).smem_optin && K % 256 == 0 &&
+        (wa & 15u) == 0)
         return launch_stream_kernel(reinterpret_cast<const void*>(proj_q8_0_kernel), x, w, out, K, N, kQ8Rows,
-                                    smem, s);
+                                    q8_smem_bytes(K), s);
     const int blocks = (N + kProjWarps - 1) / kProjWarps;
     const int grid = blocks < device_info(dev).sm_count * 16 ? blocks : device_info(dev).sm_count * 16;
     proj_generic_kernel<<<grid, kProjThreads, 0, s>>>(x, w, type, out, K, N);
