@@ -11,11 +11,12 @@
 //   (fp16 d + 32 int8): each warp copies 32 block pairs (2176 contiguous,
 //   16-byte aligned bytes) of 2 rows into its two-stage shared-memory buffer
 //   with 16-byte cp.async, one step ahead; then each lane takes one pair
-//   (68 bytes, 17 words: a word stride of 17 is bank-conflict free).  int8 ->
-//   fp32 is exact with one byte permute into 2^23 + (q + 128) and one subtract;
-//   x is staged with the 16-byte chunks of each 64-element pair group
-//   XOR-swizzled so that the lanes' chunk reads are bank-conflict free.  Per
-//   block sum(q * x) in fp32, then times d.
+//   (68 bytes, 17 words: a word stride of 17 is bank-conflict free).  x is
+//   held as four int8 pieces of a 28-bit fixed-point copy (scale 2^(e-27),
+//   e = exponent of max|x|), so a block's sum over q * x is four exact integer
+//   dot products, 4 lanes per dp4a, with no int8 -> float conversion; the
+//   block's d scales the combined value.  An x holding NaN/Inf takes the
+//   reference's float loop.
 // * proj_generic_kernel: any other shape or alignment; one warp per row with
 //   the reference's lane-strided loop.
 // * embedding_kernel: kernel_embedding_lookup (forward_baseline.cu:55-109),
@@ -133,19 +134,37 @@ constexpr int kQ8PairsPerStep = 32;                 // one block pair per lane
 constexpr int kQ8StepBytes = kQ8PairsPerStep * 68;  // 2176 B of one row
 constexpr int kQ8StageBytes = kQ8Rows * kQ8StepBytes;
 
-// x (K floats, swizzled) then per warp two stages of kQ8Rows x 2176 bytes.
+// x as four int8 pieces (K bytes each, piece-major), then per warp two stages of kQ8Rows x 2176 bytes.
 __host__ __device__ inline size_t q8_smem_bytes(int K) {
-    return (size_t)K * sizeof(float) + (size_t)kProjWarps * 2 * kQ8StageBytes;
+    return (size_t)K * 4 + (size_t)kProjWarps * 2 * kQ8StageBytes;
+}
+
+// 16-byte chunk c of a piece array lives at chunk (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)): the lanes of a
+// warp read chunk 4 pr + r of their pairs pr, and the swizzle spreads those over all eight 16-byte bank groups.
+__device__ __forceinline__ int q8_chunk_pos(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
+
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
+    return __dp4a((int)a, (int)b, c);  // signed x signed 8-bit lanes, 32-bit accumulate
+}
+
+// The reference's float loop for one row (forward_baseline.cu:205-217): the path for an x holding NaN/Inf.
+__device__ float q8_row_float(const float* __restrict__ x, const uint8_t* __restrict__ row, int nb, int lane) {
+    float acc = 0.f;
+    for (int b = lane; b < nb; b += 32) {
+        const uint8_t* blk = row + (size_t)b * 34;
+        const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        for (int j = 0; j < 32; ++j) acc = fmaf(d * (float)(int8_t)blk[2 + j], x[b * 32 + j], acc);
+    }
+    return warp_sum(acc);
 }
 
 __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __restrict__ x,
                                                                  const uint8_t* __restrict__ w,
                                                                  float* __restrict__ out, int K, int N) {
-    extern __shared__ float4 xs4[];
-    stage_x<true>(x, xs4, K);
+    extern __shared__ __align__(16) uint8_t q8_smem[];
+    __shared__ uint32_t s_max[kProjWarps];
+    __shared__ int s_bad[kProjWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t stage0 = smem_u32(reinterpret_cast<uint8_t*>(xs4) + (size_t)K * sizeof(float) +
-                                     (size_t)warp * 2 * kQ8StageBytes);
     const size_t row_bytes = (size_t)(K / 32) * 34;  // a multiple of 16 (K % 256 == 0)
     const int np = K / 64;                            // block pairs per row
     const int nj = (np + kQ8PairsPerStep - 1) / kQ8PairsPerStep;
@@ -153,6 +172,8 @@ __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __
     const int n_rp = (N + kQ8Rows - 1) / kQ8Rows;
     const int my_rp = first < n_rp ? (n_rp - first + stride - 1) / stride : 0;
     const int n_steps = my_rp * nj;
+    const uint32_t xq_s = smem_u32(q8_smem);  // piece p of x at xq_s + p * K
+    const uint32_t stage0 = xq_s + (uint32_t)K * 4u + (uint32_t)(warp * 2 * kQ8StageBytes);
 
     // step s: row pair first + (s / nj) * stride, pairs [32 (s % nj), +32) of both rows, into stage s & 1
     auto issue = [&](int st) {
@@ -169,10 +190,57 @@ __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __
         }
         cp_async_commit();  // one group per step, empty past the end
     };
+
+    // 1. max|x| and finiteness; NaN/Inf in x -> the reference's float loop, row by row
+    uint32_t m = 0;
+    int bad = 0;
+    for (int i = threadIdx.x; i < K; i += kProjThreads) {
+        const float v = __ldg(x + i);
+        bad |= !isfinite(v);
+        m = max(m, __float_as_uint(fabsf(v)));
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 0) s_max[warp] = m, s_bad[warp] = bad;
+    __syncthreads();
+    m = 0;
+    bad = 0;
+#pragma unroll
+    for (int i = 0; i < kProjWarps; ++i) m = max(m, s_max[i]), bad |= s_bad[i];
+    if (bad) {
+        for (int rp = first; rp < n_rp; rp += stride)
+            for (int i = 0; i < kQ8Rows; ++i) {
+                const int row = rp * kQ8Rows + i;
+                if (row >= N) break;
+                const float v = q8_row_float(x, w + (size_t)row * row_bytes, K / 32, lane);
+                if (lane == 0) out[row] = v;
+            }
+        return;
+    }
     issue(0);
     issue(1);
-    __syncthreads();  // x staged
+    int e = 0;
+    frexpf(__uint_as_float(m), &e);  // max|x| < 2^e (e = 0 when x == 0)
 
+    // 2. x -> X = rint(x * 2^(27-e)) (|X| <= 2^27) as balanced base-128 digits q0..q3, piece-major int8
+    for (int i = threadIdx.x; i < K; i += kProjThreads) {
+        const int X = __float2int_rn(ldexpf(__ldg(x + i), 27 - e));
+        const int q3 = ((X + 64) & 127) - 64;
+        const int X1 = (X - q3) >> 7;
+        const int q2 = ((X1 + 64) & 127) - 64;
+        const int X2 = (X1 - q2) >> 7;
+        const int q1 = ((X2 + 64) & 127) - 64;
+        const int q0 = (X2 - q1) >> 7;
+        const int pos = q8_chunk_pos(i >> 4) * 16 + (i & 15);
+        q8_smem[0 * K + pos] = (uint8_t)q0;
+        q8_smem[1 * K + pos] = (uint8_t)q1;
+        q8_smem[2 * K + pos] = (uint8_t)q2;
+        q8_smem[3 * K + pos] = (uint8_t)q3;
+    }
+    __syncthreads();
+
+    // 3. per block and row: S_p = sum q * x_p (exact, 4 lanes per dp4a), value = (S0*128+S1) * 2^14 +
+    //    (S2*128+S3), times the block's d; the row total is scaled by 2^(e-27) at the end.
     float acc[kQ8Rows];
 #pragma unroll
     for (int i = 0; i < kQ8Rows; ++i) acc[i] = 0.f;
@@ -189,34 +257,35 @@ __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __
 #pragma unroll
                 for (int k = 0; k < 17; ++k)
                     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(W[i][k]) : "r"(sp + i * kQ8StepBytes + 4 * k));
-            const float4* xg = xs4 + pr * 16;
-            const int sw = pr & 15;
-#pragma unroll
-            for (int i = 0; i < kQ8Rows; ++i)
-#pragma unroll
-                for (int k = 0; k < 17; ++k) W[i][k] ^= 0x80808080u;  // q + 128 per byte
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
-                float s[kQ8Rows][2];  // two chains per row: even / odd elements
+                uint4 xp[4][2];  // pieces 0..3 of the block's 32 x values
 #pragma unroll
-                for (int i = 0; i < kQ8Rows; ++i) s[i][0] = s[i][1] = 0.f;
+                for (int p = 0; p < 4; ++p)
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {  // elements 4 q4 .. 4 q4 + 3 of the block
-                    const float4 xv = xg[(blk * 8 + q4) ^ sw];
-                    const float xe[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int off = blk * 34 + 2 + 4 * q4 + e;  // byte offset in the pair
-#pragma unroll
-                        for (int i = 0; i < kQ8Rows; ++i)
-                            s[i][e & 1] = fmaf(s8x_to_f32(W[i][off >> 2], (uint32_t)(off & 3)), xe[e], s[i][e & 1]);
-                    }
-                }
+                    for (int h = 0; h < 2; ++h)
+                        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                                     : "=r"(xp[p][h].x), "=r"(xp[p][h].y), "=r"(xp[p][h].z), "=r"(xp[p][h].w)
+                                     : "r"(xq_s + (uint32_t)(p * K + q8_chunk_pos(4 * pr + 2 * blk + h) * 16)));
 #pragma unroll
                 for (int i = 0; i < kQ8Rows; ++i) {
-                    // d sits in the pair's bytes 0-1 (block 0) and 34-35 (block 1); undo the ^ 0x80 above
-                    const uint32_t dbits = (blk == 0 ? (W[i][0] & 0xFFFFu) : (W[i][8] >> 16)) ^ 0x8080u;
-                    acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)dbits)), s[i][0] + s[i][1], acc[i]);
+                    uint32_t q[8];  // the block's 32 int8 weights, 4 per word
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        q[g] = blk == 0 ? __funnelshift_r(W[i][g], W[i][g + 1], 16) : W[i][9 + g];
+                    int S[4];
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const uint32_t xw[8] = {xp[p][0].x, xp[p][0].y, xp[p][0].z, xp[p][0].w,
+                                                xp[p][1].x, xp[p][1].y, xp[p][1].z, xp[p][1].w};
+                        S[p] = 0;
+#pragma unroll
+                        for (int g = 0; g < 8; ++g) S[p] = dp4a(q[g], xw[g], S[p]);
+                    }
+                    // |S_p| <= 32 * 128 * 65: S0*128 + S1 and S2*128 + S3 fit in int32 (one fp32 rounding each)
+                    const float v = fmaf((float)(S[0] * 128 + S[1]), 16384.f, (float)(S[2] * 128 + S[3]));
+                    const uint32_t dbits = blk == 0 ? (W[i][0] & 0xFFFFu) : (W[i][8] >> 16);
+                    acc[i] = fmaf(__half2float(__ushort_as_half((unsigned short)dbits)), v, acc[i]);
                 }
             }
         }
@@ -225,7 +294,7 @@ __global__ void __launch_bounds__(kProjThreads) proj_q8_0_kernel(const float* __
         if (j == nj - 1) {  // row pair done
 #pragma unroll
             for (int i = 0; i < kQ8Rows; ++i) {
-                const float v = warp_sum(acc[i]);
+                const float v = ldexpf(warp_sum(acc[i]), e - 27);
                 if (lane == 0 && rp * kQ8Rows + i < N) out[rp * kQ8Rows + i] = v;
                 acc[i] = 0.f;
             }

@@ -121,3 +121,17 @@ def test_shared_memory_attribute_not_lowered():
         x = rng.standard_normal(K).astype(np.float32)
         y = hq.output_projection(torch.from_numpy(x).to("cuda:0"), dev_bytes(w), o.GGML_Q8_0, 64).cpu().numpy()
         check_close(y, o.output_projection(x, w, o.GGML_Q8_0, K, 64))
+
+
+def test_q8_0_nonfinite_x_takes_float_loop():
+    """x holding Inf/NaN: the Q8_0 kernel switches to the reference's float loop, so the non-finite pattern of
+    the logits is the reference's."""
+    rng = np.random.default_rng(12)
+    K, N = 1024, 48
+    w = make_weights(o.GGML_Q8_0, K, N, rng)
+    x = rng.standard_normal(K).astype(np.float32)
+    x[17] = np.inf
+    y = hq.output_projection(torch.from_numpy(x).to("cuda:0"), dev_bytes(w), o.GGML_Q8_0, N).cpu().numpy()
+    ref = o.output_projection(x, w, o.GGML_Q8_0, K, N)
+    assert np.array_equal(np.isnan(y), np.isnan(ref)) and np.array_equal(np.isinf(y), np.isinf(ref))
+    assert np.array_equal(np.sign(y[np.isinf(ref)]), np.sign(ref[np.isinf(ref)]))
