@@ -325,13 +325,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (n_steps > 0) issue(0);
     if (n_steps > 1) issue(1);
 
-    // 3. digit table: 16 byte values per warp, each stored to all 32 lane copies
-    {
-        const uint32_t mine = tq1_digit_word((uint32_t)(warp * 16 + (lane & 15)));
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-            reinterpret_cast<uint32_t*>(smem)[(warp * 16 + i) * 64 + lane] = __shfl_sync(0xffffffffu, mine, i);
-    }
+    // 3. chunk 0's x pieces, converted once and coalesced, into the digit-table region (free until the
+    //    table is built, after chunk 0's tables): its operand-B table and block sums then read shared memory.
+    uint32_t* xq0 = reinterpret_cast<uint32_t*>(smem);
+    const int k_chunk0 = min(in_dim, kChunkGroups * 4 * 256);
+    for (int k = tid; k < k_chunk0; k += kTcThreads) xq0[k] = x_pieces(__ldg(x + k), sh);
 
     const int g = lane >> 2, t = lane & 3;
     const uint32_t lane_off = (uint32_t)lane * 4u;
@@ -344,7 +342,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int c = 0; c * kChunkGroups < n_groups; ++c) {
         const int n_cg = min(kChunkGroups, n_groups - c * kChunkGroups);
         __syncthreads();  // the previous chunk's tables are no longer read
-        // 4. operand-B table and per-block piece sums of this chunk
+        // 4. operand-B table and per-block piece sums of this chunk (chunk 0 from xq0, later ones from x)
+        auto piece = [&](int k) { return c == 0 ? xq0[k] : x_pieces(__ldg(x + k), sh); };
         for (int idx = tid; idx < n_cg * 7 * 20; idx += kTcThreads) {
             const int j = idx / 20, mm = (idx / 4) % 5, tt = idx % 4;
             const int o = 32 * j + 8 * tt;  // chunk byte offset of lane tt's 8 bytes
@@ -356,7 +355,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int kk = tq1_slot_k(ob, 2 * mm + h, i);
-                    v[h][i] = kk < 0 ? 0u : x_pieces(__ldg(x + kbase + kk), sh);
+                    v[h][i] = kk < 0 ? 0u : piece(kbase + kk);
                 }
             uint2* dst = btab + (size_t)(j * 5 + mm) * 32 + tt;
 #pragma unroll
@@ -375,7 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int acc[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const uint32_t v = x_pieces(__ldg(x + k0 + i), sh);
+                const uint32_t v = piece(k0 + i);
 #pragma unroll
                 for (int p = 0; p < 4; ++p) acc[p] += (int)(int8_t)(v >> (8 * p));
             }
@@ -385,6 +384,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (lane == 0) qtab[bl] = make_float4((float)(acc[0] * 128 + acc[1]), (float)(acc[2] * 128 + acc[3]), 0.f, 0.f);
         }
         __syncthreads();
+        if (c == 0) {  // digit table: 16 byte values per warp, each stored to all 32 lane copies (over xq0)
+            const uint32_t mine = tq1_digit_word((uint32_t)(warp * 16 + (lane & 15)));
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                reinterpret_cast<uint32_t*>(smem)[(warp * 16 + i) * 64 + lane] = __shfl_sync(0xffffffffu, mine, i);
+            __syncthreads();
+        }
 
         // 5. decode this warp's run of the chunk's tasks.  Row sums stay in registers while the unit
         //    is the same; a segment that covers the unit's whole chunk is added to out directly, a
