@@ -5,8 +5,9 @@
 * ``build_ref()`` compiles the reference's own ``hydrogen/src/model/marlin_gemm.cu``
   where it lies (nothing is copied) together with ``ref_shim.cu`` into
   ``oracle/_ref/libref_marlin.so``.  It needs the reference tree, so it runs only
-  in the build container; the built ``.so`` travels to the GPU box with the repo
-  snapshot (``oracle/_ref/`` is git-ignored, not gpurun-ignored).
+  where that tree is present; the built ``.so`` is kept out of version control
+  (``oracle/_ref/`` is git-ignored) and is copied along with the working tree to
+  the machine that runs the GPU tests.
 
 The product library never loads either file.
 """
