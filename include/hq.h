@@ -198,6 +198,20 @@ HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
 HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
                                      int K, int N, hq_stream_t stream);
 
+/*
+ * W8A8 GEMM, the reference engine's third precision: activations quantized per
+ * element as q8(x) = (int8) trunc(clamp(x * 127, -128, 127)), int8 weights
+ * W [K][N] (k-major rows), one fp32 scale per column:
+ *   Y[m][n] = scale[n] * sum over the K/4 whole quads of k of q8(X[m][k]) W[k][n] / 127.
+ * Replaces MarlinGemmEngine::forward_cutlass_int8 / kernel_cutlass_int8_gemm
+ * (marlin_gemm.cu:327-377, 603-617); any M (the reference's acc[8] stops at 8).
+ * The int32 sums are exact and rounded once (the reference rounds an fp32
+ * running sum per quad): results within 1e-5 of max|Y| of the reference's.
+ * N % 4 == 0, K <= 65536, W 4-byte aligned; Y is used as int32 scratch first.
+ */
+HQ_API hq_status hq_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y,
+                            int M, int K, int N, hq_stream_t stream);
+
 /* GGML tensor type ids of the projection weights (gguf_parser.hpp:33-64). */
 #define HQ_GGML_F32 0
 #define HQ_GGML_Q8_0 8
@@ -286,6 +300,9 @@ HQ_API hq_status hq_marlin_forward_baseline_int4(hq_marlin_engine* e, const floa
                                                  const float* d_biases, float* d_Y, uint32_t M);
 HQ_API hq_status hq_marlin_forward_reference(hq_marlin_engine* e, const float* d_X,
                                              const float* d_W_dequant, float* d_Y_ref, uint32_t M);
+HQ_API hq_status hq_marlin_forward_cutlass_int8(hq_marlin_engine* e, const float* d_X,
+                                                const int8_t* d_W_int8, const float* d_scales,
+                                                float* d_Y, uint32_t M);
 HQ_API hq_status hq_marlin_verify_fidelity(hq_marlin_engine* e, const float* d_Y_ref,
                                            const float* d_Y_marlin, uint32_t M,
                                            double* max_abs_err, double* mse);

@@ -12,8 +12,9 @@
 //   * M up to any value (the reference silently overflows for M > 8,
 //     marlin_gemm.cu:260,304);
 //   * bandwidth_utilization_pct is relative to kPeakBandwidthGBs (B200
-//     nominal HBM3e) instead of the RTX 4070's 504 GB/s (:677).
-// forward_cutlass_int8 (marlin_gemm.hpp:112-118) is not provided.
+//     nominal HBM3e) instead of the RTX 4070's 504 GB/s (:677);
+//   * forward_cutlass_int8 sums the dp4a products exactly in int32 and rounds
+//     once (the reference rounds an fp32 running sum per 4 k), any M.
 #pragma once
 
 #include <cstddef>
@@ -75,6 +76,9 @@ public:
                              const float* d_biases, float* d_Y, uint32_t M);
 
     void forward_reference(const float* d_X, const float* d_W_dequant, float* d_Y_ref, uint32_t M);
+
+    // W8A8 path (marlin_gemm.hpp:112-118): int8 W [K][N], per-column fp32 scale.
+    void forward_cutlass_int8(const float* d_X, const int8_t* d_W_int8, const float* d_scales, float* d_Y, uint32_t M);
 
     void verify_fidelity(const float* d_Y_ref, const float* d_Y_marlin, uint32_t M, double& out_max_abs_err,
                          double& out_mse);

@@ -36,6 +36,7 @@ SIGNATURES = {
     "hq_repack_device": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "hq_tq1_0_gemv": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "hq_tq1_0_to_tile_t2": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "hq_w8_gemm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "hq_output_projection": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
     "hq_embedding_lookup": (_i, [_vp, _i, _i, _vp, _i, _i, _vp]),
     "hq_check_device_error": (_i, []),
@@ -47,6 +48,7 @@ SIGNATURES = {
     "hq_marlin_forward_marlin_int4": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _u32]),
     "hq_marlin_forward_baseline_int4": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _u32]),
     "hq_marlin_forward_reference": (_i, [_vp, _vp, _vp, _vp, _u32]),
+    "hq_marlin_forward_cutlass_int8": (_i, [_vp, _vp, _vp, _vp, _vp, _u32]),
     "hq_marlin_verify_fidelity": (_i, [_vp, _vp, _vp, _u32, ctypes.POINTER(_d), ctypes.POINTER(_d)]),
 }
 

@@ -398,6 +398,21 @@ HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* sca
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "tq1_0 conversion launch");
 }
 
+HQ_API hq_status hq_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y, int M, int K, int N,
+                            hq_stream_t stream) {
+    if (!X || !W || !scales || !Y) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (M < 0 || K <= 0 || N <= 0) return fail(HQ_ERR_INVALID_ARG, "bad size");
+    if (N % 4 || K > 65536) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "need N %% 4 == 0 and K <= 65536");
+    if (((uintptr_t)W & 3u) || ((uintptr_t)X & 3u) || ((uintptr_t)Y & 3u) || ((uintptr_t)scales & 3u))
+        return fail(HQ_ERR_MISALIGNED, "W, X, Y and scales must be 4-byte aligned");
+    int dev = 0;
+    hq_status st = check_device(&dev);
+    if (st != HQ_OK) return st;
+    if (M == 0) return HQ_OK;
+    cudaError_t e = launch_w8_gemm(X, W, scales, Y, M, K, N, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HQ_OK : cuda_fail(e, "w8 gemm launch");
+}
+
 HQ_API hq_status hq_output_projection(const float* x, const void* w, int w_type, float* logits,
                                       int embedding_dim, int vocab_size, hq_stream_t stream) {
     if (!x || !w || !logits) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");

@@ -70,6 +70,8 @@ void linear_quad(const uint32_t* src, uint32_t* dst, int K, int N, bool inverse,
 
 // TQ1_0 kernels.
 cudaError_t launch_tq1_0_gemv(const float* x, const uint8_t* w, float* out, int in_dim, int out_dim, cudaStream_t s);
+cudaError_t launch_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y, int M, int K, int N,
+                           cudaStream_t s);
 cudaError_t launch_output_projection(const float* x, const uint8_t* w, int type, float* out, int K, int N,
                                      cudaStream_t s);
 cudaError_t launch_embedding_lookup(const uint8_t* table, int type, int token_id, float* out, int K, cudaStream_t s);

@@ -94,6 +94,12 @@ void MarlinGemmEngine::forward_reference(const float* d_X, const float* d_W_dequ
                "forward_reference launch");
 }
 
+void MarlinGemmEngine::forward_cutlass_int8(const float* d_X, const int8_t* d_W_int8, const float* d_scales,
+                                            float* d_Y, uint32_t M) {
+    if (hq_w8_gemm(d_X, d_W_int8, d_scales, d_Y, (int)M, (int)config_.K, (int)config_.N, nullptr) != HQ_OK)
+        throw std::runtime_error(std::string("forward_cutlass_int8: ") + hq_last_error_string());
+}
+
 void MarlinGemmEngine::verify_fidelity(const float* d_Y_ref, const float* d_Y_marlin, uint32_t M,
                                        double& out_max_abs_err, double& out_mse) {
     const size_t count = (size_t)M * config_.N;
@@ -280,6 +286,12 @@ HQ_API hq_status hq_marlin_forward_reference(hq_marlin_engine* e, const float* d
                                              float* d_Y_ref, uint32_t M) {
     if (!e) return HQ_ERR_INVALID_ARG;
     return guarded([&] { e->e->forward_reference(d_X, d_W_dequant, d_Y_ref, M); });
+}
+
+HQ_API hq_status hq_marlin_forward_cutlass_int8(hq_marlin_engine* e, const float* d_X, const int8_t* d_W_int8,
+                                                const float* d_scales, float* d_Y, uint32_t M) {
+    if (!e) return HQ_ERR_INVALID_ARG;
+    return guarded([&] { e->e->forward_cutlass_int8(d_X, d_W_int8, d_scales, d_Y, M); });
 }
 
 HQ_API hq_status hq_marlin_verify_fidelity(hq_marlin_engine* e, const float* d_Y_ref, const float* d_Y_marlin,

@@ -22,7 +22,7 @@ from ._lib import (HQ_BF16, HQ_F16, HQ_F32, HQ_WFMT_LINEAR_T2, HQ_WFMT_LINEAR_U4
                    HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TQ1_0, HQError, check, lib)
 
 __all__ = ["HQError", "weight_bytes", "repack_host", "repack", "make_workspace", "gemm", "QuantLinear",
-           "tq1_0_gemv", "tq1_0_to_tile_t2", "output_projection", "embedding_lookup", "check_device_error",
+           "tq1_0_gemv", "tq1_0_to_tile_t2", "output_projection", "embedding_lookup", "w8_gemm", "check_device_error",
            "MarlinGemmEngine",
            "HQ_WFMT_LINEAR_U4", "HQ_WFMT_MARLIN_QUAD", "HQ_WFMT_TILE_U4", "HQ_WFMT_LINEAR_T2",
            "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0"]
@@ -122,6 +122,18 @@ def tq1_0_gemv(x: torch.Tensor, w: torch.Tensor, out_dim: int, out: torch.Tensor
     if out is None:
         out = torch.empty(out_dim, dtype=torch.float32, device=x.device)
     check(lib().hq_tq1_0_gemv(_ptr(x), _ptr(w), _ptr(out), in_dim, out_dim, _stream(stream)))
+    return out
+
+
+def w8_gemm(X: torch.Tensor, W: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None,
+            stream=None) -> torch.Tensor:
+    """forward_cutlass_int8 (marlin_gemm.cu:327-377): Y = scale * q8(X) W / 127; X fp32 [M][K], W int8 [K][N],
+    scales fp32 [N]."""
+    M, K = X.shape
+    N = W.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=X.device)
+    check(lib().hq_w8_gemm(_ptr(X), _ptr(W), _ptr(scales), _ptr(out), M, K, N, _stream(stream)))
     return out
 
 

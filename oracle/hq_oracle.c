@@ -14,6 +14,7 @@
 #include "hq_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -572,6 +573,36 @@ int hqo_embedding_lookup(const void* table, int type, int token_id, float* out, 
         } else {
             return HQO_EINVAL;
         }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------ W8A8 (int8) */
+
+static int8_t q8_of(float x) {
+    const float v = fminf(fmaxf(x * 127.0f, -128.0f), 127.0f);
+    return (int8_t)v; /* truncation toward zero */
+}
+
+int hqo_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y,
+                int M, int K, int N, int nthreads) {
+    if (!X || !W || !scales || !Y || M < 0 || K <= 0 || N <= 0) return HQO_EINVAL;
+    nthreads = set_threads(nthreads);
+    const int quads = K / 4;
+    #pragma omp parallel for num_threads(nthreads) schedule(static)
+    for (int m = 0; m < M; ++m) {
+        int8_t* xq = (int8_t*)malloc((size_t)quads * 4);
+        for (int k = 0; k < quads * 4; ++k) xq[k] = q8_of(X[(size_t)m * K + k]);
+        for (int n = 0; n < N; ++n) {
+            float acc = 0.0f;
+            for (int q = 0; q < quads; ++q) {
+                int dot = 0;
+                for (int i = 0; i < 4; ++i) dot += (int)xq[4 * q + i] * (int)W[(size_t)(4 * q + i) * N + n];
+                acc = fmaf((float)dot, 1.0f / 127.0f, acc);
+            }
+            Y[(size_t)m * N + n] = acc * scales[n];
+        }
+        free(xq);
     }
     return 0;
 }

@@ -89,6 +89,14 @@ int hqo_t2_gemm(const float* X, const uint32_t* linear_t2, const float* scales,
 int hqo_gemv_tq1_0(const float* x, const uint8_t* w, float* out, int in_dim,
                    int out_dim, int nthreads);
 
+/* kernel_cutlass_int8_gemm (marlin_gemm.cu:327-377), one output at a time:
+ * q8(x) = (int8) trunc(clamp(x * 127, -128, 127)) per element; per quad of k
+ * the 4-lane int8 dot product, added to an fp32 running sum as
+ * fmaf((float)dot, 1/127, acc) (nvcc's contraction of :369); the K % 4 tail is
+ * ignored as in the reference; Y = acc * scale[n].  W int8 [K][N]. */
+int hqo_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y,
+                int M, int K, int N, int nthreads);
+
 /* GGML tensor types taken by the projection routines (gguf_parser.hpp:33-64). */
 #define HQO_GGML_F32 0
 #define HQO_GGML_Q8_0 8

@@ -48,7 +48,7 @@ def ref_lib():
         _ref.ref_engine_create.restype = c_void_p
         _ref.ref_engine_create.argtypes = [ctypes.c_uint32] * 4
         _ref.ref_engine_destroy.argtypes = [c_void_p]
-        for f in ("ref_forward_reference", "ref_forward_marlin", "ref_forward_baseline"):
+        for f in ("ref_forward_reference", "ref_forward_marlin", "ref_forward_baseline", "ref_forward_cutlass_int8"):
             getattr(_ref, f).restype = c_int
         _ref.ref_repack_q4k_to_marlin.argtypes = [c_void_p, c_void_p, ctypes.c_uint32,
                                                   ctypes.c_uint32, ctypes.POINTER(c_double)]
@@ -240,6 +240,18 @@ def gemv_tq1_0(x, blob, in_dim, out_dim, nthreads=0):
     _ck(lib().hqo_gemv_tq1_0(_p(np.ascontiguousarray(x, np.float32)), _p(np.ascontiguousarray(blob, np.uint8)),
                              _p(out), in_dim, out_dim, nthreads), "gemv_tq1_0")
     return out
+
+
+def w8_gemm(X, W, scales, nthreads=0):
+    """kernel_cutlass_int8_gemm (marlin_gemm.cu:327-377) restated: X fp32 [M][K], W int8 [K][N], scales fp32 [N]."""
+    X = np.ascontiguousarray(X, np.float32)
+    W = np.ascontiguousarray(W, np.int8)
+    M, K = X.shape
+    N = W.shape[1]
+    Y = np.empty((M, N), np.float32)
+    _ck(lib().hqo_w8_gemm(_p(X), _p(W), _p(np.ascontiguousarray(scales, np.float32)), _p(Y), M, K, N, nthreads),
+        "w8_gemm")
+    return Y
 
 
 GGML_F32, GGML_Q8_0, GGML_BF16, GGML_TQ1_0 = 0, 8, 30, 34  # gguf_parser.hpp:33-64

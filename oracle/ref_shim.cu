@@ -94,4 +94,14 @@ int ref_forward_baseline(void* e, const float* dX, const uint32_t* dWl, const fl
     }
 }
 
+int ref_forward_cutlass_int8(void* e, const float* dX, const int8_t* dW, const float* ds, float* dY, uint32_t M) {
+    try {
+        static_cast<hydrogen::MarlinGemmEngine*>(e)->forward_cutlass_int8(dX, dW, ds, dY, M);
+        return 0;
+    } catch (const std::exception& ex) {
+        set_err(ex.what());
+        return -1;
+    }
+}
+
 }  // extern "C"

@@ -150,3 +150,15 @@ def test_projection_argument_errors():
     assert L.hq_embedding_lookup(p, _lib.HQ_GGML_F32, -1, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG
     assert L.hq_embedding_lookup(p, _lib.HQ_GGML_Q8_0, 0, p, 40, 4, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
     assert L.hq_embedding_lookup(p, 2, 0, p, 256, 4, None) == _lib.HQ_ERR_INVALID_ARG
+
+
+def test_w8_gemm_argument_errors():
+    L = _lib.lib()
+    buf = np.zeros(4096, np.uint8)
+    p = ctypes.c_void_p(buf.ctypes.data + (-buf.ctypes.data) % 16)
+    odd = ctypes.c_void_p(p.value + 2)
+    assert L.hq_w8_gemm(None, p, p, p, 1, 64, 64, None) == _lib.HQ_ERR_INVALID_ARG
+    assert L.hq_w8_gemm(p, p, p, p, 1, 64, 66, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert L.hq_w8_gemm(p, p, p, p, 1, 65540, 64, None) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert L.hq_w8_gemm(p, odd, p, p, 1, 64, 64, None) == _lib.HQ_ERR_MISALIGNED
+    assert L.hq_marlin_forward_cutlass_int8(None, p, p, p, p, 1) == _lib.HQ_ERR_INVALID_ARG

@@ -116,6 +116,19 @@ def test_projection_restatement_against_float64():
     assert np.array_equal(emb, (t[4].reshape(2, 256) * dd[:, None]).ravel().astype(np.float32))
 
 
+def test_w8_restatement_against_int64():
+    """kernel_cutlass_int8_gemm restated: against an int64 product of the same q8 activations (K % 4 tail ignored)."""
+    rng = np.random.default_rng(8)
+    M, K, N = 3, 102, 12
+    X = (rng.standard_normal((M, K)) * 0.6).astype(np.float32)
+    W = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    S = rng.uniform(0.01, 0.02, N).astype(np.float32)
+    q = np.clip(X * np.float32(127), -128, 127).astype(np.int64)  # float -> int truncates toward zero
+    kk = (K // 4) * 4
+    ref = (q[:, :kk] @ W[:kk].astype(np.int64)).astype(np.float64) / 127 * S
+    assert o.max_rel_err(o.w8_gemm(X, W, S), ref) < 1e-6
+
+
 def test_golden_config0_checksums(golden):
     import hashlib
     A, q, S = o.gen_int4_case(16, 4096, 4096, group=128, seed=0, a_dtype="f16")
