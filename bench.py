@@ -324,6 +324,33 @@ def proj_sweep(torch, L, _lib, dev, stream, peaks, args):
             "timing": "CUDA events around 10 launches after 3 warm-up, 2 rotating weight copies"}
 
 
+def w8_sweep(torch, L, _lib, dev, stream, peaks, args):
+    """The reference engine's W8A8 path (forward_cutlass_int8, marlin_gemm.cu:327-377) through hq_w8_gemm:
+    int8 W [K][N], fp32 X and per-column scales; GB/s of weight bytes, two rotating weight copies."""
+    import ctypes
+    vp = ctypes.c_void_p
+    g = torch.Generator(device=dev)
+    g.manual_seed(23)
+    rows = []
+    for M, K, N in ((1, 4096, 4096), (8, 4096, 4096), (1, 5120, 34816), (8, 5120, 34816)):
+        W = torch.randint(-128, 128, (2, K, N), dtype=torch.int8, device=dev, generator=g)
+        X = torch.randn((M, K), device=dev, generator=g) * 0.5
+        S = torch.rand(N, device=dev, generator=g) * 0.015 + 0.005
+        Y = torch.empty((M, N), device=dev)
+
+        def fn(c):
+            st = L.hq_w8_gemm(vp(X.data_ptr()), vp(W[c].data_ptr()), vp(S.data_ptr()), vp(Y.data_ptr()), M, K, N,
+                              vp(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        ms = _time_launches(torch, stream, fn, 2, reps=10)
+        rows.append({"M": M, "K": K, "N": N, "us": round(ms * 1e3, 1),
+                     "GBps": round(K * N / (ms / 1e3) / 1e9, 1)})
+        del W
+    return {"metric": "W8A8 GEMM weight GB/s (forward_cutlass_int8)", "per_gemm": rows,
+            "timing": "CUDA events around 10 calls (memset + 2 kernels each) after 3 warm-up, 2 weight copies"}
+
+
 def _ternary_tile(torch, nbytes, dev, g):
     f = torch.randint(0, 3, (nbytes, 4), dtype=torch.uint8, device=dev, generator=g)
     return (f[:, 0] | (f[:, 1] << 2) | (f[:, 2] << 4) | (f[:, 3] << 6)).contiguous()
@@ -774,12 +801,13 @@ def main():
         stack = tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args)
         hq.check_device_error()
 
-    prefill = ternary = tq1 = proj = None
+    prefill = ternary = tq1 = proj = w8 = None
     if world == 1 and not args.no_extra:
         prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
         ternary = ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
         tq1 = tq1_sweep(torch, L, _lib, dev, stream, peaks, args)
         proj = proj_sweep(torch, L, _lib, dev, stream, peaks, args)
+        w8 = w8_sweep(torch, L, _lib, dev, stream, peaks, args)
         hq.check_device_error()
 
     cpu = None
@@ -828,6 +856,8 @@ def main():
             line["tq1_0"] = tq1
         if proj is not None:
             line["output_projection"] = proj
+        if w8 is not None:
+            line["w8a8"] = w8
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
