@@ -307,6 +307,76 @@ HQ_API hq_status hq_marlin_verify_fidelity(hq_marlin_engine* e, const float* d_Y
                                            const float* d_Y_marlin, uint32_t M,
                                            double* max_abs_err, double* mse);
 
+/* ------------------------------------------------------ split-fuse batching
+ * Replaces hydrogen::SplitFuseBatcher (batcher.hpp:98-199, split_fuse.cpp):
+ * same request life cycle and step assembly; hq_batcher_execute runs the step
+ * through real hq_gemm layers where the reference's execute_step
+ * (split_fuse.cpp:196-238) simulates it.  Host-side object, not thread-safe. */
+typedef struct hq_batcher hq_batcher;
+
+/* RequestStatus (batcher.hpp:17-22). */
+enum { HQ_REQ_QUEUED = 0, HQ_REQ_RUNNING_PREFILL = 1, HQ_REQ_RUNNING_DECODE = 2, HQ_REQ_COMPLETED = 3 };
+
+/* SplitFuseConfig (batcher.hpp:66-74): the scheduling fields. */
+typedef struct hq_batcher_config {
+    uint32_t max_prefill_chunk_tokens; /* 64 in the reference */
+    uint32_t max_decode_streams;       /* 16: a sizing hint, not enforced (as in the reference) */
+    uint32_t max_batch_tokens;         /* 512 */
+} hq_batcher_config;
+
+/* BatchChunk (batcher.hpp:40-45). */
+typedef struct hq_batch_chunk {
+    uint32_t request_id, start_token, num_tokens;
+    int is_prefill;
+} hq_batch_chunk;
+
+/* FusedBatch's counters (batcher.hpp:50-56). */
+typedef struct hq_batch_info {
+    uint32_t num_decode_requests, num_prefill_tokens, total_batch_tokens;
+    double assembly_overhead_us;
+} hq_batch_info;
+
+typedef struct hq_request_state {
+    uint32_t prompt_tokens, prefill_completed_tokens, decode_tokens_generated, max_decode_tokens;
+    int status;
+} hq_request_state;
+
+/* One quantized linear layer of the stack a step runs through. */
+typedef struct hq_linear_layer {
+    const void* W;
+    hq_wfmt wfmt;
+    const void* scales;
+    hq_dtype s_dtype;
+    const float* bias; /* nullable */
+    int K, N, group;
+} hq_linear_layer;
+
+/* cfg NULL: the reference's defaults (64, 16, 512). */
+HQ_API hq_batcher* hq_batcher_create(const hq_batcher_config* cfg);
+HQ_API void hq_batcher_destroy(hq_batcher* b);
+HQ_API void hq_batcher_reset(hq_batcher* b);
+/* submit_request: returns the new request id (1, 2, ...). */
+HQ_API uint32_t hq_batcher_submit(hq_batcher* b, uint32_t prompt_tokens, uint32_t max_decode_tokens);
+/* assemble_step_batch: writes the step's chunks (decode rows first, then at
+ * most one prefill chunk) and returns their count, or -1 when max_chunks is
+ * too small (active decode streams + 1 always suffices). */
+HQ_API int hq_batcher_assemble(hq_batcher* b, hq_batch_chunk* chunks, int max_chunks, hq_batch_info* info);
+/* update_step_completion. */
+HQ_API hq_status hq_batcher_complete(hq_batcher* b, const hq_batch_chunk* chunks, int n);
+HQ_API int hq_batcher_has_work(const hq_batcher* b);
+HQ_API size_t hq_batcher_active_requests(const hq_batcher* b);
+HQ_API hq_status hq_batcher_request_state(const hq_batcher* b, uint32_t request_id, hq_request_state* out);
+/* Runs `rows` activation rows (the step's total_batch_tokens) through the
+ * layers in order with hq_gemm: layer i reads act0 (i even) or act1 as a
+ * contiguous [rows][K] array and writes the other as [rows][N]; each buffer
+ * holds rows x max(K, N) elements of a_dtype; layer i+1's K must be layer i's
+ * N; one zero-initialised workspace of hq_gemm_workspace_size for the largest
+ * layer at M = rows serves every layer (the calls are stream-ordered).  The
+ * result is in act1 for an odd number of layers, in act0 otherwise. */
+HQ_API hq_status hq_batcher_execute(hq_batcher* b, uint32_t rows, const hq_linear_layer* layers, int n_layers,
+                                    void* act0, void* act1, hq_dtype a_dtype, void* workspace, size_t ws_bytes,
+                                    hq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,16 @@ SIGNATURES = {
     "hq_check_device_error": (_i, []),
     "hq_set_launch_overlap": (None, [_i]),
     "hq_allreduce_sum": (_i, [_vp, _vp, _vp, _i, _i, _i, _sz, _u32, _i, _vp]),
+    "hq_batcher_create": (_vp, [_vp]),
+    "hq_batcher_destroy": (None, [_vp]),
+    "hq_batcher_reset": (None, [_vp]),
+    "hq_batcher_submit": (_u32, [_vp, _u32, _u32]),
+    "hq_batcher_assemble": (_i, [_vp, _vp, _i, _vp]),
+    "hq_batcher_complete": (_i, [_vp, _vp, _i]),
+    "hq_batcher_has_work": (_i, [_vp]),
+    "hq_batcher_active_requests": (_sz, [_vp]),
+    "hq_batcher_request_state": (_i, [_vp, _u32, _vp]),
+    "hq_batcher_execute": (_i, [_vp, _u32, _vp, _i, _vp, _vp, _i, _vp, _sz, _vp]),
     "hq_marlin_engine_create": (_vp, [_u32, _u32, _u32, _u32]),
     "hq_marlin_engine_destroy": (None, [_vp]),
     "hq_marlin_repack_q4k_to_marlin": (_i, [_vp, _vp, _vp, _u32, _u32, ctypes.POINTER(_d)]),
