@@ -89,11 +89,11 @@ HQ_API int hq_batcher_assemble(hq_batcher* b, hq_batch_chunk* chunks, int max_ch
         const uint32_t budget_left = b->cfg.max_batch_tokens > total ? b->cfg.max_batch_tokens - total : 0;
         const uint32_t budget = std::min(b->cfg.max_prefill_chunk_tokens, budget_left);
         if (budget > 0) {
+            if (n == max_chunks) return -1;  // before any state changes: a failed call leaves none
             Request& r = b->requests[b->prefill_queue.front() - 1];
             r.status = HQ_REQ_RUNNING_PREFILL;
             uint32_t take = std::min(r.prompt - r.prefilled, budget);
             take = std::min(take, b->cfg.max_prefill_chunk_tokens);
-            if (n == max_chunks) return -1;
             chunks[n++] = hq_batch_chunk{r.id, r.prefilled, take, 1};
             n_prefill = take;
             total += take;
@@ -107,9 +107,10 @@ HQ_API int hq_batcher_assemble(hq_batcher* b, hq_batch_chunk* chunks, int max_ch
 
 HQ_API hq_status hq_batcher_complete(hq_batcher* b, const hq_batch_chunk* chunks, int n) {
     if (!b || (n > 0 && !chunks) || n < 0) return HQ_ERR_INVALID_ARG;
+    for (int i = 0; i < n; ++i)  // validate the whole step first: an invalid one changes nothing
+        if (chunks[i].request_id == 0 || chunks[i].request_id > b->requests.size()) return HQ_ERR_INVALID_ARG;
     for (int i = 0; i < n; ++i) {
         const hq_batch_chunk& c = chunks[i];
-        if (c.request_id == 0 || c.request_id > b->requests.size()) return HQ_ERR_INVALID_ARG;
         Request& r = b->requests[c.request_id - 1];
         if (c.is_prefill) {
             r.prefilled += c.num_tokens;

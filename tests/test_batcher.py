@@ -81,3 +81,23 @@ def test_batch_budget_limits_prefill():
     fb = b.assemble_step_batch()
     assert fb.num_decode_requests == 18 and fb.num_prefill_tokens == 2 and fb.total_batch_tokens == 20
     b.close()
+
+
+def test_failed_calls_change_nothing():
+    """A too-small chunk buffer (assemble) or an unknown request id (complete) fails without changing state."""
+    import ctypes
+    from nebula_b200 import _lib
+    from nebula_b200.batcher import _Chunk, _Info, QUEUED
+    L = _lib.lib()
+    b = SplitFuseBatcher(64, 16, 512)
+    b.submit_request(100, 2)
+    buf = (_Chunk * 1)()
+    assert L.hq_batcher_assemble(b._h, buf, 0, ctypes.byref(_Info())) == -1
+    assert b.request_state(1)["status"] == QUEUED
+    fb = b.assemble_step_batch()
+    bad = (_Chunk * 2)(_Chunk(fb.chunks[0].request_id, 0, fb.chunks[0].num_tokens, 1), _Chunk(99, 0, 1, 0))
+    assert L.hq_batcher_complete(b._h, bad, 2) == _lib.HQ_ERR_INVALID_ARG
+    assert b.request_state(1)["prefill_completed_tokens"] == 0
+    b.update_step_completion(fb)
+    assert b.request_state(1)["prefill_completed_tokens"] == 64
+    b.close()
