@@ -89,10 +89,13 @@ HQ_API size_t hq_weight_bytes(hq_wfmt fmt, int K, int N);
 
 /* Workspace bytes that hq_gemm needs for this problem (a multiple of 256;
  * 0 when none is needed, in which case workspace may be NULL).  The workspace
- * holds re-tiled weights for the reference layouts and the tensor-core
- * kernel's split-K state.  Zero-fill it once before first use
- * (hq_workspace_init); calls leave any counters in it at zero again, so no
- * per-call memset. */
+ * holds re-tiled weights for the reference layouts and the decode kernel's
+ * split state: one arrival counter per 128-column group and the fp32 partial
+ * tiles of groups shared by two SMs.  Zero-fill it once before first use
+ * (hq_workspace_init); every call leaves the counters at zero again, so no
+ * per-call memset.  A call that fails with HQ_ERR_TIMEOUT may leave counters
+ * set: zero-fill again before the next call.  One workspace per stream: calls
+ * that may run at the same time need different workspaces. */
 HQ_API size_t hq_gemm_workspace_size(int M, int N, int K, int group, hq_wfmt wfmt);
 HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t stream);
 
@@ -143,12 +146,17 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype,
  * point allocates nothing and calls no allocating routine.
  *   - Limit: a problem whose hq_gemm_workspace_size exceeds
  *     HQ_NOALLOC_SCRATCH_BYTES fails with HQ_ERR_WORKSPACE_TOO_SMALL (reference
- *     layouts need K*N/2 bytes for int4, K*N/4 for ternary; tile-order weights
- *     need none).
- *   - The first call on a device, with that device current, looks up the
- *     array's device address and zero-fills it (synchronously); make that
- *     first call before any stream capture.  The array then stays on that
- *     device until the process exits.
+ *     layouts need K*N/2 bytes for int4, K*N/4 for ternary, plus the decode
+ *     kernel's split state of about 2.4 MB on a 148-SM B200).
+ *   - The first call on a device that needs scratch, with that device
+ *     current, looks up the array's device address, zero-fills it and waits
+ *     for the device (cudaDeviceSynchronize); make that first call before any
+ *     stream capture.
+ *   - The array is part of the library's device code: it occupies
+ *     HQ_NOALLOC_SCRATCH_BYTES on every device where the library's module is
+ *     loaded (from the first call under lazy module loading, the CUDA default;
+ *     from context creation with CUDA_MODULE_LOADING=EAGER) until the process
+ *     exits.
  *   - All calls on a device share the array, which keeps the previous call's
  *     contents; calls whose GPU work overlaps (different streams, several host
  *     threads) race on it, so keep them on one stream.

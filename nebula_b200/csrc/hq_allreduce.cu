@@ -124,9 +124,12 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const __grid_cons
         s_ok = wait_all(my_flags, 0, p.world, p.epoch, p.err) ? 1 : 0;
     }
     __syncthreads();
-    if (!s_ok) return;
 
-    // 2. this rank's slice: sum over ranks in order, push to every rank
+    // 2. this rank's slice: sum over ranks in order, push to every rank.  After a
+    // timed-out barrier (error word set) the pushes are skipped, but the CTA still
+    // counts itself in step 3, so the arrival counter stays in step with the epoch
+    // and the next call on these flags is not wedged.
+    if (s_ok) {
     const size_t per = (p.vecs + p.world - 1) / p.world;
     const size_t v0 = (size_t)p.rank * per;
     const size_t v1 = v0 + per < p.vecs ? v0 + per : p.vecs;
@@ -175,6 +178,8 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const __grid_cons
         }
     }
 
+    }
+
     // 3. the last CTA of this rank to finish its pushes tells every rank; all wait
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const __grid_cons
             __threadfence_system();
             for (int j = 0; j < p.world; ++j) st_release_sys(p.flags[j] + 1 * kArMaxWorld + p.rank, p.epoch);
         }
-        wait_all(my_flags, 1, p.world, p.epoch, p.err);
+        if (s_ok) wait_all(my_flags, 1, p.world, p.epoch, p.err);
     }
 }
 

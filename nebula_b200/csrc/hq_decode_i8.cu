@@ -1,0 +1,617 @@
+// hq_decode_i8.cu -- decode GEMM (M <= 16) on the integer tensor cores:
+// int4 codes x fp16/bf16 activations through mma.sync s8 x s8 -> s32.
+//
+// Replaces, for int4 weights, 16-bit activations and no bias, the reference's
+// kernel_marlin_gemm_int4_templated / _dynamic and its memset + atomicAdd
+// split-K (hydrogen/src/model/marlin_gemm.cu:130-322, :556-601).
+//
+// Why integers: a decode GEMM reads every weight byte once, so its speed is set
+// by how few instructions turn a byte of codes into tensor-core operands.
+// Expanding int4 into fp16 pairs costs ~9 instructions per 32-bit word.  Here:
+//   * A weight byte pair of nibbles becomes two signed bytes 16 q (q = u - 8):
+//     hi = (w & 0xF0F0F0F0) ^ 0x80808080 is the high nibble of every byte as
+//     16 u - 128 = 16 q (one LOP3); the low nibbles take a shift first.  Both
+//     classes carry the same factor 16, so they share one accumulator, and no
+//     offset correction is needed (the MMA sees q itself).
+//   * Activations are converted once per call by x_prep_kernel into two
+//     signed-byte pieces of a 15-bit fixed-point copy: x = 2^-s (256 h + l)
+//     with s per (token, scale group) chosen from the group's max|x|, h in
+//     [-64, 64], l in [-128, 127].  Piece h of token m is MMA column 2m, piece
+//     l column 2m + 1, so a lane holds both pieces of one token and combines
+//     them exactly in int32 (256 c0 + c1).  The pieces are stored per k-block
+//     in the order in which each lane's B fragments read them (one 16-byte
+//     shared-memory load per lane per k-block and 4-token tile).
+//   * The exact int32 sums are scaled once per scale group:
+//     y += scale[g][n] * 2^-s / 16 * (256 c0 + c1), fp32.
+// The fixed-point copy keeps 15 bits relative to the largest |x| of each
+// (token, scale group): results stay within ~1e-5 of max|y| of the fp32
+// dequantize-then-matmul.  A group holding Inf/NaN activations makes that
+// token's outputs NaN.
+//
+// Streaming is the same as the fp16 decode kernel (hq_decode.cu): one CTA per
+// SM over an equal share of the tile-order byte stream, a bulk-copy ring fed
+// by one producer warp (codes and scales before griddepcontrol.wait, the
+// activation pieces after it), eight consumer warps each owning one 16-column
+// strip, and strip groups shared between CTAs finished by the last CTA to
+// arrive (partials summed in CTA order; counters reset by that CTA).
+#include "hq_common.cuh"
+#include "hq_internal.h"
+#include "hq_layout.h"
+
+#include <cstring>
+#include <type_traits>
+#include <utility>
+
+#ifndef HQ_DECODE_I8_CTAS_PER_SM
+#define HQ_DECODE_I8_CTAS_PER_SM 1
+#endif
+#ifndef HQ_DECODE_I8_RING_KB
+#define HQ_DECODE_I8_RING_KB 200
+#endif
+
+namespace hq {
+
+namespace {
+
+constexpr int kNC = 16;  // consumer warps: warps w and w + 8 own strip w of a strip group
+constexpr int kProducerWarps = 2;  // warp kNC issues the code copy; both share the small operands
+constexpr int kProducerWarp = kNC;
+constexpr int kThreads = (kNC + kProducerWarps) * 32;
+constexpr int kUPS = 8;        // k-blocks per stage (32 KB of full-group codes: one bulk copy)
+constexpr int kBatch = 4;      // k-blocks a consumer warp keeps in flight
+constexpr int kTokTile = 4;    // tokens per MMA n-tile (two pieces each)
+constexpr int kTileBytes = 512;  // piece bytes of one k-block and one 4-token tile
+constexpr int kCtasPerSm = HQ_DECODE_I8_CTAS_PER_SM;
+constexpr int kRingBudget = HQ_DECODE_I8_RING_KB * 1024;
+constexpr int kPairBar = 1;  // named barrier of all consumer warps
+constexpr int kHalfBar = 2;  // named barrier of the first eight consumer warps
+constexpr int kPrepThreads = 256;  // 16 token slots x 16 threads
+
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+constexpr int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); }
+
+template <int NT, typename ST>
+struct RingI8 {
+    static constexpr int kW = kUPS * kGroupStrips * 512;  // codes
+    static constexpr int kXUnit = NT * kTileBytes;       // pieces of one k-block
+    static constexpr int kX = kW;
+    static constexpr int kSUnit = kGroupCols * (int)sizeof(ST);  // one scale row of the group's columns
+    static constexpr int kS = kX + kUPS * kXUnit;
+    static constexpr int kXS = kS + kUPS * kSUnit;  // x scales: 16 token slots x fp32 per scale group
+    static constexpr int kBytes = align_up(kXS + kUPS * 64, 128);
+    static constexpr int kStages = clampi(kRingBudget / kBytes, 2, 8);
+    static constexpr int kPair = 2 * 8 * NT * 32 * 8;  // two buffers of half 1's sums (float2 per lane)
+    static constexpr int kSmem = kStages * kBytes + kPair + 128 + 2 * kStages * 8 + 16;
+};
+
+struct alignas(16) I8Params {
+    const uint8_t* W;
+    const void* S;
+    const int8_t* pieces;  // [K/64][NT*4 tokens][2][4][16] (workspace)
+    const float* xscale;   // [K/group][16] 2^-s per (group, token slot) (workspace)
+    void* C;
+    unsigned* err;
+    unsigned* counters;  // [NSG]
+    float2* partials;    // [G][2][8 strips][NT * 32]
+    int M, N, K, group;
+    int early_weights;
+};
+
+struct Span {
+    int sg, kb, n;
+};
+
+struct Walker {
+    int sg, kb, left, KB, ups;
+    __device__ __forceinline__ Walker(long long u, long long end, int KB_, int ups_)
+        : sg((int)(u / KB_)), kb((int)(u % KB_)), left((int)(end - u)), KB(KB_), ups(ups_) {}
+    __device__ __forceinline__ bool next(Span& s) {
+        if (left <= 0) return false;
+        int n = KB - kb < ups ? KB - kb : ups;
+        if (n > left) n = left;
+        s.sg = sg;
+        s.kb = kb;
+        s.n = n;
+        left -= n;
+        kb += n;
+        if (kb == KB) {
+            kb = 0;
+            ++sg;
+        }
+        return true;
+    }
+};
+
+__device__ __forceinline__ long long range_begin(long long U, int G, int c) { return U * c / G; }
+
+__device__ __forceinline__ int cta_of(long long u, long long U, int G) {
+    int c = (int)((u * G) / U);
+    while (c + 1 < G && range_begin(U, G, c + 1) <= u) ++c;
+    while (c > 0 && range_begin(U, G, c) > u) --c;
+    return c;
+}
+
+// D (16x8 s32) += A (16x32 s8) x B (32x8 s8).
+__device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 16 q as signed bytes from the high / low nibble of every byte of a tile word.
+__device__ __forceinline__ uint32_t q16_hi(uint32_t w) { return lop3<(0xF0 & 0xCC) ^ 0xAA>(w, 0xF0F0F0F0u, 0x80808080u); }
+__device__ __forceinline__ uint32_t q16_lo(uint32_t w) { return lop3<(0xF0 & 0xCC) ^ 0xAA>(w << 4, 0xF0F0F0F0u, 0x80808080u); }
+
+// Activation pieces.  One CTA per scale group, 16 threads per token slot, 8
+// consecutive k per thread.  Writes the pieces of token slots [0, slots) (zero
+// beyond M) and 2^-s of all 16 slots of the group.
+template <typename AT>
+__global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restrict__ A, int M, int K, int group,
+                                                              int slots, int8_t* __restrict__ pieces,
+                                                              float* __restrict__ xscale) {
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    // A may come from the previous kernel, and that kernel may still read the
+    // pieces of the previous call.
+    pdl_wait();
+    const int gi = blockIdx.x;
+    const int m = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+    const int oct = group / 8;
+    const AT* row = A + (size_t)m * K + (size_t)gi * group;
+    float mx = 0.f;
+    int bad = 0;
+    if (m < M) {
+        for (int o = l16; o < oct; o += 16) {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + 8 * o);
+            const AT* e = reinterpret_cast<const AT*>(&v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float f = to_f32(e[i]);
+                bad |= !isfinite(f);
+                mx = fmaxf(mx, fabsf(f));
+            }
+        }
+    }
+#pragma unroll
+    for (int d = 8; d >= 1; d >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, d);
+    }
+    // x * 2^s < 2^14 for every |x| <= mx, so |x_fixed| <= 2^14 and h = (x_fixed + 128) >> 8 <= 64.
+    int s = 0;
+    float xs = 0.f;
+    if (bad) {
+        xs = __int_as_float(0x7fc00000);
+    } else if (mx > 0.f) {
+        s = 13 - ilogbf(mx);
+        xs = ldexpf(1.f, -s);
+    }
+    if (l16 == 0) xscale[(size_t)gi * 16 + m] = m < M ? xs : 0.f;
+    if (m >= slots) return;
+    for (int o = l16; o < oct; o += 16) {
+        int xf[8];
+        if (m < M && !bad) {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + 8 * o);
+            const AT* e = reinterpret_cast<const AT*>(&v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xf[i] = (int)rintf(ldexpf(to_f32(e[i]), s));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xf[i] = 0;
+        }
+        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+        // byte j of word A holds element {0,2,1,3}[j], of word B element {4,6,5,7}[j]
+        constexpr int kOrder[8] = {0, 2, 1, 3, 4, 6, 5, 7};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int v = xf[kOrder[j]];
+            const int h = (v + 128) >> 8;
+            const int l = v - (h << 8);
+            hw[j >> 2] |= (uint32_t)(h & 0xFF) << (8 * (j & 3));
+            lw[j >> 2] |= (uint32_t)(l & 0xFF) << (8 * (j & 3));
+        }
+        const int k0 = gi * group + 8 * o;
+        const int kb = k0 >> 6, t = (k0 >> 4) & 3, hh = (k0 >> 3) & 1;
+        int8_t* tile = pieces + (size_t)kb * slots * 128;
+        uint32_t* ph = reinterpret_cast<uint32_t*>(tile + ((m * 2 + 0) * 4 + t) * 16);
+        uint32_t* pl = reinterpret_cast<uint32_t*>(tile + ((m * 2 + 1) * 4 + t) * 16);
+        ph[hh] = hw[0];
+        ph[2 + hh] = hw[1];
+        pl[hh] = lw[0];
+        pl[2 + hh] = lw[1];
+    }
+}
+
+template <int NT, typename ST, typename OT>
+__global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_constant__ I8Params p) {
+    using L = RingI8<NT, ST>;
+    constexpr int kStages = L::kStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+    float2* pair_buf = reinterpret_cast<float2*>(ring + kStages * L::kBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * L::kBytes + L::kPair);
+    uint64_t* empty = full + kStages;
+    volatile int* s_last = reinterpret_cast<volatile int*>(empty + kStages);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const TileGeom geo(p.K, p.N, 4);
+    const int KB = geo.KB;
+    const long long U = geo.units();
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    const long long u_begin = range_begin(U, G, c), u_end = range_begin(U, G, c + 1);
+    const int upg = p.group / kBlockK;  // k-blocks per scale group
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1 + 32 * kProducerWarps);  // the bulk copy's expect-tx + one cp.async arrival per producer lane
+            mbar_init(&empty[i], kNC);
+        }
+        fence_mbarrier_init();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        pdl_launch_dependents();
+    }
+    __syncthreads();
+
+    if (warp >= kProducerWarp) {
+        // --------------------------------------------------------- producers
+        // A warp holding more than a few DRAM-latency cp.async per lane stalls
+        // its issue; four warps share them so that none does.
+        const int pl = (warp - kProducerWarp) * 32 + lane;  // producer lane 0..127
+        const uint64_t pol = l2_policy_evict_first();
+        const uint8_t* Sb = reinterpret_cast<const uint8_t*>(p.S);
+        auto stage_ptr = [&](int it) { return ring + (it % kStages) * L::kBytes; };
+        // Codes (one bulk copy) and weight-scale rows (16-byte cp.async spread over
+        // the lanes) of stage `it`: no earlier kernel writes them.
+        auto issue_w = [&](int it, const Span& d) {
+            const int slot = it % kStages;
+            uint8_t* st = stage_ptr(it);
+            const int width = geo.width(d.sg);
+            const int s_chunks = width * kStripCols * (int)sizeof(ST) / 16;  // 16-byte pieces of one scale row
+            const uint32_t wbytes = (uint32_t)d.n * (uint32_t)width * 512u;
+            const int g_first = d.kb / upg, ng = (d.kb + d.n - 1) / upg - g_first + 1;
+            if (pl == 0) {
+                mbar_arrive_expect_tx(&full[slot], wbytes);
+                bulk_g2s_hint(st, p.W + geo.unit_offset((long long)d.sg * KB + d.kb), wbytes, &full[slot], pol);
+            }
+            for (int i = pl; i < ng * s_chunks; i += 32 * kProducerWarps) {
+                const int r = i / s_chunks, cidx = i - r * s_chunks;
+                const size_t off = (size_t)(g_first + r) * p.N + (size_t)d.sg * kGroupCols;
+                cp_async16(st + L::kS + r * L::kSUnit + 16 * cidx, Sb + off * sizeof(ST) + 16 * cidx);
+            }
+        };
+        // Activation pieces and their scales (written by the preceding kernel), then
+        // every lane's arrival once its copies of the stage have landed.
+        auto issue_x = [&](int it, const Span& d) {
+            const int slot = it % kStages;
+            uint8_t* st = stage_ptr(it);
+            const int g_first = d.kb / upg, ng = (d.kb + d.n - 1) / upg - g_first + 1;
+            const int p_chunks = d.n * NT * kTileBytes / 16;
+            const int8_t* psrc = p.pieces + (size_t)d.kb * NT * kTileBytes;
+            for (int i = pl; i < p_chunks; i += 32 * kProducerWarps) cp_async16(st + L::kX + 16 * i, psrc + 16 * i);
+            for (int i = pl; i < ng * 4; i += 32 * kProducerWarps)
+                cp_async16(st + L::kXS + 16 * i, p.xscale + (size_t)g_first * 16 + 4 * i);
+            cp_async_mbar_arrive(&full[slot]);
+        };
+        Walker wk(u_begin, u_end, KB, kUPS);
+        Span d;
+        Span pend[kStages];
+        int it = 0;
+        if (!p.early_weights) pdl_wait();
+        while (it < kStages && wk.next(d)) {
+            issue_w(it, d);
+            if (p.early_weights)
+                pend[it] = d;
+            else
+                issue_x(it, d);
+            ++it;
+        }
+        if (p.early_weights) {
+            pdl_wait();
+            for (int j = 0; j < it; ++j) issue_x(j, pend[j]);
+        }
+        while (wk.next(d)) {
+            const int slot = it % kStages;
+            int w_ok = 1;
+            if (lane == 0) w_ok = mbar_wait(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
+            w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+            if (!w_ok) break;
+            issue_w(it, d);
+            issue_x(it, d);
+            ++it;
+        }
+        if (lane == 0)
+            for (int j = it - kStages < 0 ? 0 : it - kStages; j < it; ++j)
+                mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1u, p.err);
+        __syncwarp();
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    // Two warps per strip: half 0 takes the first kBatch k-blocks of every
+    // stage, half 1 the rest; their sums meet in shared memory when a strip
+    // group is done.
+    pdl_wait();
+    const int g = lane >> 2, t = lane & 3;
+    const int sl = warp & 7, half = warp >> 3;
+    OT* C = reinterpret_cast<OT*>(p.C);
+    float facc[NT][2];
+    int iacc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        facc[j][0] = facc[j][1] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) iacc[j][i] = 0;
+    }
+
+    // Exact integer sums of one scale group -> fp32 (scale row gl of the stage).
+    auto flush_ints = [&](const uint8_t* stage, int gl) {
+        const int nl = sl * kStripCols + g;
+        const uint8_t* sp = stage + L::kS + gl * L::kSUnit;
+        const float s0 = to_f32(*reinterpret_cast<const ST*>(sp + nl * sizeof(ST)));
+        const float s1 = to_f32(*reinterpret_cast<const ST*>(sp + (nl + 8) * sizeof(ST)));
+        const float* xs = reinterpret_cast<const float*>(stage + L::kXS + gl * 64);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            const float f = xs[kTokTile * j + t] * 0.0625f;  // 2^-s / 16
+            const int v0 = iacc[j][0] * 256 + iacc[j][1];
+            const int v1 = iacc[j][2] * 256 + iacc[j][3];
+            facc[j][0] = fmaf((float)v0, s0 * f, facc[j][0]);
+            facc[j][1] = fmaf((float)v1, s1 * f, facc[j][1]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) iacc[j][i] = 0;
+        }
+    };
+
+    auto store_pair = [&](int sg, int j, float v0, float v1) {
+        const int n = sg * kGroupCols + sl * kStripCols + g;
+        const int tok = kTokTile * j + t;
+        if (tok < p.M) {
+            C[(size_t)tok * p.N + n] = from_f32<OT>(v0);
+            C[(size_t)tok * p.N + n + 8] = from_f32<OT>(v1);
+        }
+    };
+
+    const int first_sg = (int)(u_begin / KB);
+    int pend_sg[2] = {-1, -1};  // strip groups handed to the fixup, by slot
+    int nflush = 0;
+    // Strip group `sg` is done for this CTA: half 1 hands its sums to half 0,
+    // which stores the group or, when other CTAs share it, writes the partial
+    // and lets thread 0 count the arrival (the last arriver sums after the loop).
+    auto flush_group = [&](int sg) {
+        float2* xch = pair_buf + ((nflush & 1) * 8 + sl) * (NT * 32);
+        ++nflush;
+        if (half == 1) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) xch[j * 32 + lane] = make_float2(facc[j][0], facc[j][1]);
+        }
+        named_bar_sync(kPairBar, kNC * 32);
+        if (half == 0) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const float2 v = xch[j * 32 + lane];
+                facc[j][0] += v.x;
+                facc[j][1] += v.y;
+            }
+            const int width = geo.width(sg);
+            const long long g0 = (long long)sg * KB, g1 = g0 + KB;
+            if (g0 >= u_begin && g1 <= u_end) {
+                if (sl < width)
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) store_pair(sg, j, facc[j][0], facc[j][1]);
+            } else {
+                const int slot = sg == first_sg ? 0 : 1;
+                float2* mine = p.partials + (((size_t)c * 2 + slot) * 8 + sl) * (NT * 32);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) mine[j * 32 + lane] = make_float2(facc[j][0], facc[j][1]);
+                named_bar_sync(kHalfBar, 8 * 32);
+                if (threadIdx.x == 0) {
+                    __threadfence();  // cumulative: orders every half-0 partial before the arrival
+                    const int c_first = cta_of(g0, U, G), c_last = cta_of(g1 - 1, U, G);
+                    const unsigned old = atomicAdd(&p.counters[sg], 1u);
+                    s_last[slot] = old == (unsigned)(c_last - c_first);
+                }
+                pend_sg[slot] = sg;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) facc[j][0] = facc[j][1] = 0.f;
+    };
+
+    bool waits_ok = true;
+    Walker wk(u_begin, u_end, KB, kUPS);
+    Span d;
+    int it = 0, cur = -1;
+    while (wk.next(d)) {
+        if (d.sg != cur) {
+            if (cur >= 0) flush_group(cur);
+            cur = d.sg;
+        }
+        const int slot = it % kStages;
+        if (waits_ok) waits_ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+        const uint8_t* stage = ring + slot * L::kBytes;
+        const int width = geo.width(d.sg);
+        const int b0 = half * kBatch;  // this warp's k-blocks of the stage: [b0, min(b0 + kBatch, n))
+        const int bn = d.n - b0 < kBatch ? d.n - b0 : kBatch;
+        if (sl < width && bn > 0) {
+            const uint32_t unit_bytes = (uint32_t)width * 512u;
+            const uint8_t* wbase = stage + (b0 * (int)unit_bytes) + sl * 512 + lane * 16;
+            const int g_stage = d.kb / upg;
+            int gl = (d.kb + b0) / upg - g_stage;                     // scale row of k-block b0
+            int gend = ((d.kb + b0) / upg + 1) * upg - (d.kb + b0);  // k-blocks of the batch to its group's end
+            uint4 wv[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+                wv[u] = u < bn ? *reinterpret_cast<const uint4*>(wbase + u * unit_bytes) : make_uint4(0u, 0u, 0u, 0u);
+            const uint8_t* xbase = stage + L::kX + b0 * L::kXUnit + lane * 16;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (u >= bn) break;
+                const uint32_t l0 = q16_lo(wv[u].x), l1 = q16_lo(wv[u].z), l2 = q16_lo(wv[u].y), l3 = q16_lo(wv[u].w);
+                const uint32_t h0 = q16_hi(wv[u].x), h1 = q16_hi(wv[u].z), h2 = q16_hi(wv[u].y), h3 = q16_hi(wv[u].w);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xbase + u * L::kXUnit + j * kTileBytes);
+                    imma_16832(iacc[j], l0, l1, l2, l3, xv.x, xv.y);
+                    imma_16832(iacc[j], h0, h1, h2, h3, xv.z, xv.w);
+                }
+                if (u + 1 == gend) {
+                    flush_ints(stage, gl);
+                    ++gl;
+                    gend += upg;
+                } else if (u + 1 == bn) {
+                    flush_ints(stage, gl);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        ++it;
+    }
+    if (cur >= 0) flush_group(cur);
+
+    // Strip groups shared with other CTAs that this CTA reached last: sum every
+    // sharer's partial in CTA order, store, and reset the group's counter.
+    if (half == 0) {
+        named_bar_sync(kHalfBar, 8 * 32);  // thread 0's arrival results are visible
+#pragma unroll
+        for (int slot = 0; slot < 2; ++slot) {
+            const int sg = pend_sg[slot];
+            if (sg < 0 || !s_last[slot]) continue;
+            __threadfence();
+            const long long g0 = (long long)sg * KB, g1 = g0 + KB;
+            const int c_first = cta_of(g0, U, G), c_last = cta_of(g1 - 1, U, G);
+            float2 sum[NT];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) sum[j] = make_float2(0.f, 0.f);
+            for (int q = c_first; q <= c_last; ++q) {
+                const int qslot = (int)(range_begin(U, G, q) / KB) == sg ? 0 : 1;
+                const float2* src = p.partials + (((size_t)q * 2 + qslot) * 8 + sl) * (NT * 32);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const float2 v = __ldcg(src + j * 32 + lane);
+                    sum[j].x += v.x;
+                    sum[j].y += v.y;
+                }
+            }
+            if (sl < geo.width(sg))
+#pragma unroll
+                for (int j = 0; j < NT; ++j) store_pair(sg, j, sum[j].x, sum[j].y);
+            if (threadIdx.x == 0) p.counters[sg] = 0u;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace hq
+
+namespace hq {
+
+namespace {
+
+using I8Fn = void (*)(I8Params);
+
+template <int NT, typename ST, typename OT>
+std::pair<I8Fn, int> i8_kernel() {
+    return {decode_i8_kernel<NT, ST, OT>, RingI8<NT, ST>::kSmem};
+}
+
+template <typename ST, typename OT>
+std::pair<I8Fn, int> pick_nt(int NT) {
+    switch (NT) {
+        case 1: return i8_kernel<1, ST, OT>();
+        case 2: return i8_kernel<2, ST, OT>();
+        case 3: return i8_kernel<3, ST, OT>();
+        default: return i8_kernel<4, ST, OT>();
+    }
+}
+
+template <typename ST>
+std::pair<I8Fn, int> pick_out(DType c, int NT) {
+    if (c == DType::F16) return pick_nt<ST, __half>(NT);
+    if (c == DType::BF16) return pick_nt<ST, __nv_bfloat16>(NT);
+    return pick_nt<ST, float>(NT);
+}
+
+std::pair<I8Fn, int> select_i8(const GemmArgs& a) {
+    const int NT = (a.M + kTokTile - 1) / kTokTile;
+    if (a.s_dtype == DType::F16) return pick_out<__half>(a.c_dtype, NT);
+    if (a.s_dtype == DType::BF16) return pick_out<__nv_bfloat16>(a.c_dtype, NT);
+    return pick_out<float>(a.c_dtype, NT);
+}
+
+size_t pieces_bytes(int K) { return (size_t)(K / kBlockK) * 4 * kTileBytes; }
+size_t xscale_bytes(int K) { return ((size_t)(K / kBlockK) * 64 + 255) & ~(size_t)255; }
+
+}  // namespace
+
+bool decode_i8_supported(const GemmArgs& a) {
+    if (a.wbits != 4 || a.bias || a.M < 1 || a.M > 16) return false;
+    if (a.a_dtype != DType::F16 && a.a_dtype != DType::BF16) return false;
+    if (a.c_dtype != a.a_dtype && a.c_dtype != DType::F32) return false;
+    return a.group % kBlockK == 0 && a.K % a.group == 0;
+}
+
+size_t decode_i8_extra_bytes(int K) { return pieces_bytes(K) + xscale_bytes(K); }
+
+cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t split = decode_split_bytes(a.N, a.K, 4, dev);
+    if (!a.ws || a.ws_bytes < split + decode_i8_extra_bytes(a.K)) return cudaErrorInvalidValue;
+    const int NT = (a.M + kTokTile - 1) / kTokTile;
+    int8_t* pieces = reinterpret_cast<int8_t*>(a.ws + split);
+    float* xscale = reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K));
+
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+
+    // 1. activation pieces
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3((unsigned)(a.K / a.group));
+    pc.blockDim = dim3(kPrepThreads);
+    pc.stream = a.stream;
+    pc.attrs = pdl;
+    pc.numAttrs = 1;
+    if (a.a_dtype == DType::F16)
+        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__half>, static_cast<const __half*>(a.A), a.M, a.K, a.group,
+                               NT * kTokTile, pieces, xscale);
+    else
+        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(a.A), a.M, a.K,
+                               a.group, NT * kTokTile, pieces, xscale);
+    if (e != cudaSuccess) return e;
+
+    // 2. the GEMM
+    const std::pair<I8Fn, int> k = select_i8(a);
+    e = ensure_smem_attr(reinterpret_cast<const void*>(k.first), dev, k.second);
+    if (e != cudaSuccess) return e;
+    I8Params p;
+    memset(&p, 0, sizeof p);
+    p.W = a.W;
+    p.S = a.S;
+    p.pieces = pieces;
+    p.xscale = xscale;
+    p.C = a.C;
+    p.err = device_error_word(dev);
+    p.counters = reinterpret_cast<unsigned*>(a.ws);
+    p.partials = reinterpret_cast<float2*>(a.ws + decode_counters_bytes(a.N));
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    p.group = a.group;
+    p.early_weights = (early_weights && !a.weights_just_written) ? 1 : 0;
+    const long long U = TileGeom(a.K, a.N, 4).units();
+    const long long G = (long long)device_info(dev).sm_count * kCtasPerSm;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(U < G ? U : G));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)k.second;
+    cfg.stream = a.stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k.first, p);
+}
+
+}  // namespace hq

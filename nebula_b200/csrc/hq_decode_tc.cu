@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
         bool ok = true;
         for (int it = 0; it < n_iters; ++it) {
             const int slot = it % kStages;
-            if (lane == 0 && ok) ok = mbar_wait<256>(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
+            if (lane == 0 && ok) ok = mbar_wait(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
             uint8_t* st = ring + slot * L::kBytes;
             if (lane == 0) {
                 const uint32_t wbytes = 2 * unit_bytes;
@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
                 const int slot = it % kStages, b = it & 1;
                 // The set's four warps expanded this k-block (so the stage landed,
                 // and the set's A and D buffers of stage it-2 are drained).
-                if (ok) ok = mbar_wait<64>(&a_full[2 * u + b], (uint32_t)(it >> 1) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_full[2 * u + b], (uint32_t)(it >> 1) & 1u, p.err);
                 tc_fence_after();
                 const uint32_t xs = smem_u32(ring + slot * L::kBytes + L::kX + u * L::kXUnit);
 #pragma unroll
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
         bool ok = true;
         auto drain = [&](int i, float sc) {
             const int b = i & 1;
-            if (ok) ok = mbar_wait<128>(&d_full[2 * set + b], (uint32_t)(i >> 1) & 1u, p.err);
+            if (ok) ok = mbar_wait(&d_full[2 * set + b], (uint32_t)(i >> 1) & 1u, p.err);
             __syncwarp();
             tc_fence_after();
             uint32_t v[8];
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_tc_kernel(const __grid_con
         };
         for (int it = 0; it < n_iters; ++it) {
             const int slot = it % kStages, b = it & 1;
-            if (ok) ok = mbar_wait<128>(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+            if (ok) ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
             __syncwarp();
             tc_fence_after();
             const uint8_t* st = ring + slot * L::kBytes;

@@ -12,11 +12,16 @@
 // The array is a file-scope __device__ variable of HQ_NOALLOC_SCRATCH_BYTES.
 // Host code only sees a stand-in symbol for it, so the device address is
 // looked up with cudaGetSymbolAddress, once per device, on the first call
-// made with that device current; that first call also zero-fills the array
-// (hq_gemm's workspace contract: zero before first use, counters left at zero
-// by every call).  The first call on a device should therefore come before
-// any stream capture.  Once this set-up has run, the array stays resident on
-// that device until the process exits.
+// made with that device current.  That first call also zero-fills the array
+// (hq_gemm's workspace contract: the decode kernel keeps per-column-group
+// arrival counters there, zero before first use and left at zero by every
+// call) and waits for the fill to finish with cudaDeviceSynchronize, so that
+// no kernel of this or any later call, on any stream, can overtake it.  The
+// first call on a device must therefore come before any stream capture.
+// The array belongs to the library's device code: it is resident on every
+// device where the library's module is loaded (at the first call under lazy
+// module loading, at context creation with CUDA_MODULE_LOADING=EAGER) until
+// the process exits.
 //
 // Every call on a device shares the one array and finds there whatever the
 // previous call left.  Calls whose GPU work overlaps (concurrent streams,
@@ -60,6 +65,9 @@ hq_status scratch_address(void** out) {
             return noalloc_fail(HQ_ERR_CUDA, buf);
         }
         e = cudaMemset(p, 0, kScratchBytes);
+        // cudaMemset on device memory may return before the fill is done, and
+        // it is not ordered with the caller's (possibly non-blocking) stream.
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
             char buf[160];
             snprintf(buf, sizeof buf, "hq_gemm_noalloc: zero-filling the scratch array failed: %s",
@@ -81,6 +89,8 @@ extern "C" HQ_API hq_status hq_gemm_noalloc(const void* A, hq_dtype a_dtype, con
                                             hq_stream_t stream) {
     // Bad shapes and formats get hq_gemm's own diagnostics (workspace size 0 here).
     const size_t need = hq_gemm_workspace_size(M, N, K, group, wfmt);
+    if (need == 0)  // nothing to hold: no set-up, no scratch
+        return hq_gemm(A, a_dtype, Wq, wfmt, scales, s_dtype, bias, C, c_dtype, M, N, K, group, nullptr, 0, stream);
     if (need > hq::kScratchBytes) {
         char buf[200];
         snprintf(buf, sizeof buf,

@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                 for (int kb = 0; kb < KB; ++kb, ++it) {
                     const int ab = it % kABufs, slot = it % kStages;
                     // a_full implies full: the dequant warps saw the stage land first.
-                    if (ok) ok = mbar_wait<64>(&a_full[ab], (uint32_t)(it / kABufs) & 1u, p.err);
+                    if (ok) ok = mbar_wait(&a_full[ab], (uint32_t)(it / kABufs) & 1u, p.err);
                     tc_fence_after();
                     const uint32_t xs = smem_u32(ring + slot * L::kStage);
 #pragma unroll
@@ -205,8 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 if ((it & 1) != set) continue;
                 const int slot = it % kStages, ab = it % kABufs;
-                if (ok) ok = mbar_wait<128>(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
-                if (ok) ok = mbar_wait<128>(&a_empty[ab], ((uint32_t)(it / kABufs) & 1u) ^ 1u, p.err);
+                if (ok) ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+                if (ok) ok = mbar_wait(&a_empty[ab], ((uint32_t)(it / kABufs) & 1u) ^ 1u, p.err);
                 __syncwarp();
                 tc_fence_after();
                 const uint8_t* st = ring + slot * L::kStage;
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                 if (lane == 0) mbar_arrive(&a_full[ab]);
             }
             // Epilogue of this tile: tokens [128 set, 128 set + 128) of column cl.
-            if (ok) ok = mbar_wait<256>(acc_full, (uint32_t)tc & 1u, p.err);
+            if (ok) ok = mbar_wait(acc_full, (uint32_t)tc & 1u, p.err);
             __syncwarp();
             tc_fence_after();
             const int col = sg * TM + cl;

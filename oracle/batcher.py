@@ -1,7 +1,8 @@
 """Restatement of hydrogen::SplitFuseBatcher's scheduling (batcher.hpp:98-199, split_fuse.cpp:70-193).
 
 TEST INFRASTRUCTURE ONLY: tests drive nebula_b200's native batcher and this restatement with the same
-submissions and compare every step.  Nothing in the product library imports it.
+submissions and compare every step (on CPU), and, where a GPU is visible, the native batcher against the
+reference's own compiled scheduler (``CompiledRefSplitFuse``).  Nothing in the product library imports it.
 """
 from __future__ import annotations
 
@@ -63,3 +64,67 @@ class RefSplitFuse:
 
     def has_active_work(self):
         return bool(self.prefill_queue or self.decode)
+
+
+class CompiledRefSplitFuse:
+    """The reference's own hydrogen::SplitFuseBatcher (split_fuse.cpp, compiled where it lies into
+    oracle/_ref/libref_batcher.so by oracle/build.py).  Its constructor allocates device memory, so it
+    exists only where a GPU is visible.  Same surface as RefSplitFuse."""
+
+    def __init__(self, max_prefill_chunk_tokens=64, max_decode_streams=16, max_batch_tokens=512):
+        import ctypes
+        import os
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref", "libref_batcher.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = ctypes.CDLL(path)
+        u32, vp = ctypes.c_uint32, ctypes.c_void_p
+        L.refb_create.restype, L.refb_create.argtypes = vp, [u32, u32, u32]
+        L.refb_destroy.argtypes = [vp]
+        L.refb_submit.restype, L.refb_submit.argtypes = u32, [vp, u32, u32]
+        L.refb_assemble.restype = ctypes.c_int
+        L.refb_assemble.argtypes = [vp, ctypes.POINTER(u32), ctypes.c_int, ctypes.POINTER(u32)]
+        L.refb_complete_last.restype, L.refb_complete_last.argtypes = ctypes.c_int, [vp]
+        L.refb_has_work.restype, L.refb_has_work.argtypes = ctypes.c_int, [vp]
+        L.refb_active.restype, L.refb_active.argtypes = ctypes.c_uint64, [vp]
+        L.refb_state.restype, L.refb_state.argtypes = ctypes.c_int, [vp, u32, ctypes.POINTER(u32)]
+        L.refb_last_error.restype = ctypes.c_char_p
+        self._L, self._ct = L, ctypes
+        self._h = L.refb_create(max_prefill_chunk_tokens, max_decode_streams, max_batch_tokens)
+        if not self._h:
+            raise RuntimeError(L.refb_last_error().decode())
+
+    def close(self):
+        if self._h:
+            self._L.refb_destroy(self._h)
+            self._h = None
+
+    def submit_request(self, prompt, max_decode):
+        return int(self._L.refb_submit(self._h, prompt, max_decode))
+
+    def assemble_step_batch(self):
+        """(chunks [(rid, start, n, is_prefill)], n_decode, n_prefill_tokens, total_tokens)"""
+        ct = self._ct
+        cap = int(self._L.refb_active(self._h)) + 2
+        buf = (ct.c_uint32 * (4 * cap))()
+        info = (ct.c_uint32 * 3)()
+        n = self._L.refb_assemble(self._h, buf, cap, info)
+        if n < 0:
+            raise RuntimeError("refb_assemble failed")
+        chunks = [(buf[4 * i], buf[4 * i + 1], buf[4 * i + 2], bool(buf[4 * i + 3])) for i in range(n)]
+        return chunks, info[0], info[1], info[2]
+
+    def update_step_completion(self):
+        """Advance past the batch assembled last (the reference keeps it)."""
+        if self._L.refb_complete_last(self._h) != 0:
+            raise RuntimeError(self._L.refb_last_error().decode())
+
+    def has_active_work(self):
+        return bool(self._L.refb_has_work(self._h))
+
+    def request_state(self, rid):
+        out = (self._ct.c_uint32 * 5)()
+        if self._L.refb_state(self._h, rid, out) != 0:
+            return None
+        return {"prompt_tokens": out[0], "prefill_completed_tokens": out[1], "decode_tokens_generated": out[2],
+                "max_decode_tokens": out[3], "status": out[4]}

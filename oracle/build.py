@@ -2,12 +2,15 @@
 
 * ``build_oracle()`` compiles this project's CPU restatement ``hq_oracle.c`` into
   ``oracle/liboracle.so`` with gcc.
-* ``build_ref()`` compiles the reference's own ``hydrogen/src/model/marlin_gemm.cu``
-  where it lies (nothing is copied) together with ``ref_shim.cu`` into
-  ``oracle/_ref/libref_marlin.so``.  It needs the reference tree, so it runs only
-  where that tree is present; the built ``.so`` is kept out of version control
-  (``oracle/_ref/`` is git-ignored) and is copied along with the working tree to
-  the machine that runs the GPU tests.
+* ``build_ref()`` compiles the reference's own sources where they lie (nothing is
+  copied): ``hydrogen/src/model/marlin_gemm.cu`` with ``ref_shim.cu`` into
+  ``oracle/_ref/libref_marlin.so``, and ``hydrogen/src/batcher/split_fuse.cpp``
+  with ``ref_batcher_shim.cpp`` into ``oracle/_ref/libref_batcher.so``.  It needs
+  the reference tree: the directory named by ``HQ_REFERENCE_ROOT``, else a
+  checkout named ``reference`` beside this repository.  Where neither exists
+  (the GPU machine) the prebuilt libraries are used; they are kept out of
+  version control (``oracle/_ref/`` is git-ignored) and travel with the working
+  tree.
 
 The product library never loads either file.
 """
@@ -19,7 +22,14 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("HQ_REFERENCE_ROOT", "/root/reference")
+ROOT = os.path.dirname(HERE)
+
+
+def ref_root() -> str:
+    """The reference tree: $HQ_REFERENCE_ROOT, else a checkout named `reference` beside this repository."""
+    return os.environ.get("HQ_REFERENCE_ROOT") or os.path.join(os.path.dirname(ROOT), "reference")
+
+
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 
 
@@ -43,7 +53,11 @@ def build_oracle(force: bool = False) -> str:
 
 
 def ref_sources() -> list[str]:
-    return [os.path.join(REF_ROOT, "hydrogen", "src", "model", "marlin_gemm.cu")]
+    return [os.path.join(ref_root(), "hydrogen", "src", "model", "marlin_gemm.cu")]
+
+
+def ref_batcher_sources() -> list[str]:
+    return [os.path.join(ref_root(), "hydrogen", "src", "batcher", "split_fuse.cpp")]
 
 
 def build_ref(force: bool = False) -> str | None:
@@ -65,7 +79,26 @@ def build_ref(force: bool = False) -> str | None:
         cmd = [NVCC, "-std=c++20", "-O3", "--use_fast_math", "--expt-relaxed-constexpr",
                "-gencode", "arch=compute_100a,code=sm_100a",
                "-Xcompiler", "-fPIC", "-shared",
-               "-I", os.path.join(REF_ROOT, "hydrogen", "include"),
+               "-I", os.path.join(ref_root(), "hydrogen", "include"),
+               srcs[0], shim, "-o", out + ".tmp", "-lcudart"]
+        subprocess.run(cmd, check=True)
+        os.replace(out + ".tmp", out)
+    build_ref_batcher(force)
+    return out
+
+
+def build_ref_batcher(force: bool = False) -> str | None:
+    """Compile the reference split-fuse scheduler (split_fuse.cpp, C++20 as hydrogen/CMakeLists.txt builds
+    it) with the C shim; None when neither the reference tree nor a prebuilt library is present."""
+    out = os.path.join(HERE, "_ref", "libref_batcher.so")
+    srcs = ref_batcher_sources()
+    if not all(os.path.exists(s) for s in srcs):
+        return out if os.path.exists(out) else None
+    shim = os.path.join(HERE, "ref_batcher_shim.cpp")
+    if force or _stale(out, srcs + [shim, __file__]):
+        os.makedirs(os.path.dirname(out), exist_ok=True)
+        cmd = [NVCC, "-std=c++20", "-O2", "-x", "cu", "-gencode", "arch=compute_100a,code=sm_100a",
+               "-Xcompiler", "-fPIC", "-shared", "-I", os.path.join(ref_root(), "hydrogen", "include"),
                srcs[0], shim, "-o", out + ".tmp", "-lcudart"]
         subprocess.run(cmd, check=True)
         os.replace(out + ".tmp", out)

@@ -61,3 +61,64 @@ def test_batcher_drives_real_gemm_steps():
         assert steps < 200
     assert len(rows_seen) > 3  # the steps ran at several different M
     b.close()
+
+
+def _pin_to_reference(cfg, arrivals, max_steps=20000):
+    """Drive the native scheduler and the reference's compiled SplitFuseBatcher with the same submissions;
+    every assembled batch and every request's final state must be equal."""
+    from nebula_b200.batcher import SplitFuseBatcher
+    from oracle.batcher import CompiledRefSplitFuse
+    nat, ref = SplitFuseBatcher(*cfg), CompiledRefSplitFuse(*cfg)
+    n_sub = 0
+    try:
+        for step in range(max_steps):
+            for prompt, dec in arrivals.get(step, []):
+                assert nat.submit_request(prompt, dec) == ref.submit_request(prompt, dec)
+                n_sub += 1
+            if not nat.has_active_work() and step > max(arrivals, default=0):
+                assert not ref.has_active_work()
+                break
+            assert nat.has_active_work() == ref.has_active_work()
+            b = nat.assemble_step_batch()
+            rc, n_dec, n_pre, total = ref.assemble_step_batch()
+            got = [(c.request_id, c.start_token, c.num_tokens, c.is_prefill) for c in b.chunks]
+            assert got == rc, step
+            assert (b.num_decode_requests, b.num_prefill_tokens, b.total_batch_tokens) == (n_dec, n_pre, total)
+            nat.update_step_completion(b)
+            ref.update_step_completion()
+        for rid in range(1, n_sub + 1):
+            st, r = nat.request_state(rid), ref.request_state(rid)
+            keys = ("prompt_tokens", "prefill_completed_tokens", "decode_tokens_generated", "max_decode_tokens",
+                    "status")
+            assert r is not None and tuple(st[k] for k in keys) == tuple(r[k] for k in keys), rid
+    finally:
+        nat.close()
+        ref.close()
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_scheduler_pinned_to_reference_split_fuse(seed):
+    """split_fuse.cpp:84-193 compiled from the reference tree (oracle/_ref/libref_batcher.so): random
+    arrival traces over several configurations, including clamps below the default 64-token chunk."""
+    import os
+    if not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle",
+                                       "_ref", "libref_batcher.so")):
+        pytest.skip("reference scheduler not built (oracle/build.py needs the reference tree)")
+    rng = np.random.default_rng(100 + seed)
+    cfg = [(64, 16, 512), (64, 16, 80), (32, 8, 40), (1, 4, 3), (64, 4, 70), (128, 16, 512), (16, 2, 17),
+           (64, 16, 16)][seed]
+    arrivals = {}
+    for _ in range(int(rng.integers(5, 40))):
+        step = int(rng.integers(0, 200))
+        arrivals.setdefault(step, []).append((int(rng.integers(0, 1500)), int(rng.integers(0, 40))))
+    _pin_to_reference(cfg, arrivals)
+
+
+def test_scheduler_pinned_to_reference_1500_token_observation():
+    """The reference's own H10 scenario: 8 decode streams, then a 1500-token observation."""
+    import os
+    if not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle",
+                                       "_ref", "libref_batcher.so")):
+        pytest.skip("reference scheduler not built (oracle/build.py needs the reference tree)")
+    arrivals = {0: [(1, 10_000)] * 8, 3: [(1500, 5)]}
+    _pin_to_reference((64, 16, 512), arrivals, max_steps=200)

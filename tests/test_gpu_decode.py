@@ -69,13 +69,14 @@ def test_reference_layouts_give_identical_results(M):
 
 @pytest.mark.parametrize("K,N", [(17408, 5120), (5120, 34816), (256, 48)])
 def test_decode_is_deterministic(K, N):
-    """Split-K over a thread-block cluster reduces in rank order: repeated calls are bitwise equal."""
+    """Strip groups split between CTAs are summed in CTA order by whichever CTA arrives last:
+    repeated calls (sharing one workspace, whose counters every call leaves at zero) are bitwise equal."""
     g, M = 128, 16
     A, q, S = o.gen_int4_case(M, K, N, group=g, seed=5)
     W = cuda(o.pack_tile(q, 4), None)
     At, St = cuda(A, "f16"), cuda(S, "f16")
-    assert _lib.lib().hq_gemm_workspace_size(M, N, K, g, _lib.HQ_WFMT_TILE_U4) == 0  # decode needs none
-    ys = [hq.gemm(At, W, St, N=N, group=g).clone() for _ in range(3)]
+    ws = hq.make_workspace(M, N, K, g, _lib.HQ_WFMT_TILE_U4, At.device)
+    ys = [hq.gemm(At, W, St, N=N, group=g, workspace=ws).clone() for _ in range(3)]
     torch.cuda.synchronize()
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
     ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=g)
@@ -110,9 +111,10 @@ def test_launch_overlap_chain_matches_serial():
 
 @pytest.mark.parametrize("name,K,N", [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816),
                                       ("down", 17408, 5120)])
-@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
 def test_decode_27b_shapes(name, K, N, M):
-    """BASELINE config 1 shapes at full size (the oracle runs these in well under a second)."""
+    """BASELINE config 1 at full size: every shape at every M of the decode sweep (the oracle runs
+    these in well under a second each)."""
     A, q, S = o.gen_int4_case(M, K, N, group=128, seed={"qkv": 1, "o": 2, "gate_up": 3, "down": 4}[name] * 100 + M, a_dtype="f16")
     ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=128)
     W = hq.repack(cuda(o.pack_linear_u4(q), None), _lib.HQ_WFMT_LINEAR_U4, _lib.HQ_WFMT_TILE_U4, K, N)

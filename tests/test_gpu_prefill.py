@@ -64,9 +64,10 @@ def test_prefill_is_deterministic():
 
 @pytest.mark.parametrize("name,K,N", [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816),
                                       ("down", 17408, 5120)])
-@pytest.mark.parametrize("M", [512, 2048])
+@pytest.mark.parametrize("M", [512, 2048, 8192])
 def test_prefill_27b_shapes(name, K, N, M):
-    """BASELINE config 2 shapes (bf16 activations and scales), checked on a sample of rows."""
+    """BASELINE config 2 at every shape and token count (bf16 activations and scales), checked on a
+    sample of rows."""
     rng = np.random.default_rng(M + K + N)
     A, q, S = o.gen_int4_case(M, K, N, group=128, seed={"qkv": 1, "o": 2, "gate_up": 3, "down": 4}[name],
                               a_dtype="bf16")
@@ -75,3 +76,19 @@ def test_prefill_27b_shapes(name, K, N, M):
     rows = np.sort(rng.choice(M, size=24, replace=False))
     ref = o.w4_gemm(np.ascontiguousarray(A[rows]), o.pack_linear_u4(q), S, group=128)
     assert o.max_rel_err(y[rows], ref) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("name,K,N", [("qkv", 5120, 7168), ("o", 5120, 5120), ("gate_up", 5120, 34816),
+                                      ("down", 17408, 5120)])
+def test_prefill_ternary_27b_shapes(name, K, N):
+    """BASELINE config 3 at M = 2048 on the 27B shapes (2-bit ternary codes, fp16 activations and
+    scales ~U(0.01, 0.05)): the tensor-core path, checked on a sample of rows."""
+    M = 2048
+    rng = np.random.default_rng(K + N + 7)
+    A, t, S = o.gen_ternary_case(M, K, N, group=128, seed={"qkv": 11, "o": 12, "gate_up": 13, "down": 14}[name],
+                                 a_dtype="f16")
+    W = hq.repack(cuda(o.pack_linear_t2(t)), _lib.HQ_WFMT_LINEAR_T2, _lib.HQ_WFMT_TILE_T2, K, N)
+    y = run(A, W, S, N, 128, "f16", wfmt=_lib.HQ_WFMT_TILE_T2)
+    rows = np.sort(rng.choice(M, size=24, replace=False))
+    ref = o.t2_gemm(np.ascontiguousarray(A[rows]), o.pack_linear_t2(t), S, group=128)
+    assert o.max_rel_err(y[rows], ref) <= TOL["f16"]

@@ -186,3 +186,58 @@ def test_q8_pair_layout_and_dp4a_sums():
         v = np.ldexp(float((S[0] * 128 + S[1]) * 2 ** 14 + (S[2] * 128 + S[3])), e - 27) * float(d[blk])
         ref = float(d[blk]) * float(q[32 * blk:32 * blk + 32].astype(np.float64) @ x[32 * blk:32 * blk + 32])
         assert abs(v - ref) <= 1e-6 * (abs(ref) + 1e-3)
+
+
+# ---------------------------------------------------------------------------
+# Integer-MMA decode (csrc/hq_decode_i8.cu): tile-order codes -> signed bytes
+# 16 q, activation pieces in the prep kernel's order, m16n8k32 s8 fragments.
+
+_PIECE_POS = [0, 2, 1, 3, 8, 10, 9, 11, 4, 6, 5, 7, 12, 14, 13, 15]  # byte j of a lane's 16 B <- k offset
+
+
+def _s8(words):
+    return np.asarray(words, np.uint32).view(np.uint8).view(np.int8).astype(np.int64)
+
+
+def _mma_m16n8k32(a, b):
+    """a: 32 lanes x 4 regs (4 s8 each); b: 32 lanes x 2 regs -> D[16][8] (the PTX fragment layout)."""
+    A = np.zeros((16, 32), np.int64)
+    B = np.zeros((32, 8), np.int64)
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        for r, (row, k0) in enumerate([(g, 4 * t), (g + 8, 4 * t), (g, 16 + 4 * t), (g + 8, 16 + 4 * t)]):
+            A[row, k0:k0 + 4] = _s8([a[lane][r]])
+        B[4 * t:4 * t + 4, g] = _s8([b[lane][0]])
+        B[16 + 4 * t:16 + 4 * t + 4, g] = _s8([b[lane][1]])
+    return A @ B
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_int8_decode_fragments_give_16q_dot_x(seed):
+    rng = np.random.default_rng(seed)
+    K, N, M = 64, 16, 4
+    q = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    tile = o.pack_tile(q, 4).view(np.uint32)  # one chunk: 16 columns x 64 k
+    xf = rng.integers(-16384, 16385, size=(M, K))  # fixed-point activations
+    h = (xf + 128) >> 8
+    l = xf - 256 * h
+    assert h.min() >= -128 and h.max() <= 127 and l.min() >= -128 and l.max() <= 127
+    # prep kernel layout: [(m*2 + piece)*4 + t][16 bytes]
+    pieces = np.zeros((M * 2 * 4, 16), np.int8)
+    for m in range(M):
+        for p, arr in enumerate((h, l)):
+            for t in range(4):
+                pieces[(m * 2 + p) * 4 + t] = [arr[m, 16 * t + _PIECE_POS[j]] for j in range(16)]
+    xbytes = pieces.reshape(-1).view(np.uint32).reshape(32, 4)  # lane -> its 16 bytes
+    lo = lambda w: (((w << 4) & 0xFFFFFFFF) & 0xF0F0F0F0) ^ 0x80808080  # noqa: E731
+    hi = lambda w: (w & 0xF0F0F0F0) ^ 0x80808080  # noqa: E731
+    a_lo, a_hi = [], []
+    for lane in range(32):
+        x, y, z, w = (int(v) for v in tile[4 * lane:4 * lane + 4])
+        a_lo.append([lo(x), lo(z), lo(y), lo(w)])
+        a_hi.append([hi(x), hi(z), hi(y), hi(w)])
+    D = _mma_m16n8k32(a_lo, [xbytes[lane][0:2] for lane in range(32)]) + \
+        _mma_m16n8k32(a_hi, [xbytes[lane][2:4] for lane in range(32)])
+    want = 16 * (q.astype(np.int64).T @ xf.T)  # [n][m]
+    for m in range(M):
+        assert np.array_equal(256 * D[:, 2 * m] + D[:, 2 * m + 1], want[:, m])

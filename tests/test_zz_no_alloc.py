@@ -87,3 +87,40 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert st == _lib.HQ_ERR_WORKSPACE_TOO_SMALL
     msg = L.hq_last_error_string().decode()
     assert "scratch" in msg and str(_lib.HQ_NOALLOC_SCRATCH_BYTES) in msg
+
+
+_FIRST_CALL_ON_SIDE_STREAM = r"""
+import ctypes, sys
+import numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from nebula_b200 import _lib, hq
+from oracle import oracle as o
+M, K, N, g = 8, 1024, 512, 128
+A, q, S = o.gen_int4_case(M, K, N, group=g, seed=77, a_dtype="f16")
+lin = o.pack_linear_u4(q)
+dev = lambda x: torch.from_numpy(np.ascontiguousarray(x).view(np.uint8).reshape(-1)).to("cuda:0")
+At = torch.from_numpy(A).to("cuda:0").half(); St = torch.from_numpy(S).to("cuda:0").half(); Wt = dev(lin)
+side = torch.cuda.Stream()  # non-blocking: not ordered with the legacy default stream
+y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda:0")
+with torch.cuda.stream(side):
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    _lib.check(_lib.lib().hq_gemm_noalloc(vp(At), _lib.HQ_F16, vp(Wt), _lib.HQ_WFMT_LINEAR_U4, vp(St), _lib.HQ_F16,
+                                          None, vp(y), _lib.HQ_F16, M, N, K, g, ctypes.c_void_p(side.cuda_stream)))
+side.synchronize()
+err = o.max_rel_err(y.float().cpu().numpy(), o.w4_gemm(A, lin, S, group=g))
+print("max_rel_err", err)
+sys.exit(0 if np.isfinite(err) and err <= 1e-2 else 1)
+"""
+
+
+def test_noalloc_first_call_on_a_side_stream_in_a_fresh_process():
+    """The first call of a process does the set-up (address lookup and zero fill).  Made on a
+    non-blocking stream, the GEMM it launches must still see the array fully zero-filled and
+    the re-tiled weights intact."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _FIRST_CALL_ON_SIDE_STREAM, root], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
