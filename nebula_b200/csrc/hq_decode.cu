@@ -3,37 +3,31 @@
 // Replaces kernel_marlin_gemm_int4_templated / _dynamic and the memset +
 // atomicAdd split-K of the reference (hydrogen/src/model/marlin_gemm.cu:130-322,
 // :556-601).  Design for B200:
-//   * Byte-balanced persistent split ("stream-K").  The tile order stores the
-//     weights as units (strip group sg, k-block kb) in sg-major order, each one
-//     contiguous span, so the whole tensor is one byte stream.  The grid has
-//     one CTA per SM and CTA c takes units [U c / G, U (c+1) / G): every SM
-//     streams the same number of bytes whatever the shape, and a launch costs
-//     one wave.  Shared memory (~105 KB) and registers are sized so that two
-//     CTAs fit an SM: the next GEMM on the stream (programmatic dependent
-//     launch) becomes resident beside this one and streams its first stages
-//     while this one finishes, so back-to-back GEMMs keep HBM busy.
-//   * One producer warp moves a stage -- up to 4 k-blocks (int4) / 8 (ternary)
-//     of one strip group, 16 KB of codes -- with one 1-D bulk copy (TMA engine,
-//     L2 evict-first), plus each k-block's activation tile (one 2-D TMA box of
-//     64 k x 8 or 16 rows, 128-byte swizzled, rows >= M zero-filled) and its
-//     scale (and bias) row, into a ring of several stages.  Weights and scales
-//     are requested before griddepcontrol.wait, activations after it.
-//   * Eight consumer warps; warp w owns strip w (16 output columns) of the
-//     stage's strip group, so its partial sums never leave registers until the
-//     group is done.  A lane's 16 bytes of a k-block are its A fragments for
-//     four m16n8k16 steps: codes are OR-ed into an fp16/bf16 exponent pattern
-//     and one packed subtract gives exact q; fp32 accumulation, the group
-//     scale applied in fp32 per k-block.
-//   * A strip group wholly inside one CTA's range is stored straight from
-//     registers.  A group split between CTAs (at most the first and last of a
-//     CTA's range) is finished by the last CTA to reach it: every sharer
-//     writes its fp32 partial tile to the workspace and bumps the group's
-//     counter; the CTA that brings the counter to the number of sharers sums
-//     the partials in CTA order (deterministic: the same order whichever CTA
-//     arrives last), writes C and resets the counter.  No CTA ever waits on
-//     another, no memset, no float atomics.
+//   * Work = strip groups of 128 output columns.  A thread-block cluster of cs
+//     CTAs (cs in {1,2,4,8,10,12}, chosen from the measured cluster occupancy
+//     so the grid fills the GPU) owns one strip
+//     group; CTA r of the cluster streams the group's k-blocks
+//     [r KB/cs, (r+1) KB/cs), which the tile order stores as one contiguous
+//     byte span.  One producer warp moves it with 1-D bulk copies (TMA engine)
+//     into a 4-stage shared-memory ring, two 64-k blocks per stage, together
+//     with each block's activation tile (one 2-D TMA box of 16 rows x 64 k,
+//     128-byte swizzled, rows >= M zero-filled) and group-scale row, so the
+//     consumer loop reads only shared memory.  L2 evict-first on the weights.
+//   * Four consumer warps each own two 16-column strips.  A lane's 16 bytes
+//     are its A fragments for four m16n8k16 steps: codes are OR-ed into an
+//     fp16/bf16 exponent pattern (one LOP3 per pair) and fed to the tensor
+//     cores; one packed subtract per pair gives exact q.  fp32
+//     accumulation; the group scale is applied in fp32 once per group within a
+//     stage (never rounded into the weight).
+//   * Split-K reduction through distributed shared memory: each CTA leaves its
+//     fp32 partial in its own shared memory, and after a cluster barrier CTA r
+//     sums 1/cs of the tile over the cs CTAs in rank order (deterministic) and
+//     writes C.  No workspace, no atomics, no memset.
+//   * Programmatic dependent launch: each CTA lets the next kernel on the
+//     stream start immediately; weights and scales (which no earlier kernel
+//     writes) are requested before griddepcontrol.wait, activations after it,
+//     so the next GEMM's weight stream overlaps this GEMM's tail.
 #include "hq_common.cuh"
-#include "hq_decode_frag.cuh"
 #include "hq_internal.h"
 #include "hq_layout.h"
 #include "hq_tmap.h"
@@ -42,145 +36,209 @@
 #include <cstring>
 #include <type_traits>
 
-#ifndef HQ_DECODE_CTAS_PER_SM
-#define HQ_DECODE_CTAS_PER_SM 1
-#endif
-#ifndef HQ_DECODE_RING_KB
-#define HQ_DECODE_RING_KB 200
-#endif
-#ifndef HQ_DECODE_TC_ROUTE
-#define HQ_DECODE_TC_ROUTE 1
-#endif
-#ifndef HQ_DECODE_I8
-#define HQ_DECODE_I8 1
-#endif
-
 namespace hq {
 
 namespace {
 
-using frag::ComputeType;
-using frag::lds_scale;
-using frag::WFrag;
-using frag::XFrag;
-using frag::XFragF32;
-
-constexpr int kNC = 16;  // consumer warps: warps w and w + 8 own strip w of a strip group
-constexpr int kProducerWarps = 2;  // warp kNC issues the code copy; both share the small operands
-constexpr int kProducerWarp = kNC;
-constexpr int kThreads = (kNC + kProducerWarps) * 32;
+constexpr int kConsumerWarps = 4;
+constexpr int kStripsPerWarp = 2;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kUPS = 2;  // 64-k blocks per stage
 constexpr int kMaxRows = 16;
-constexpr int kCtasPerSm = HQ_DECODE_CTAS_PER_SM;
-constexpr int kRingBudget = HQ_DECODE_RING_KB * 1024;
-constexpr int kPairBar = 1;  // named barrier of all consumer warps
-constexpr int kHalfBar = 2;  // named barrier of the first eight consumer warps
-constexpr int kBatch = 4;     // k-blocks a consumer warp keeps in flight
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
-constexpr int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); }
 
-// Shared-memory layout of one ring stage.
-template <int WBITS, int MT, typename AT, typename ST, bool kBias>
-struct Ring {
+// Shared-memory layout of one pipeline stage.
+template <int WBITS, typename AT, typename ST, bool kBias>
+struct Stage {
     static constexpr int kCB = WBITS == 4 ? 512 : 256;
-    static constexpr int kUPS = WBITS == 4 ? 8 : 16;          // k-blocks per stage
-    static constexpr int kW = kUPS * kGroupStrips * kCB;     // codes of a full-width stage: 32 KB, one bulk copy
-    static constexpr bool kXTma = sizeof(AT) == 2;           // 16-bit activations: 128-byte XOR-swizzled rows
-    static constexpr int kXRows = 8 * MT;
-    static constexpr int kXRowBytes = kBlockK * (int)sizeof(AT);
-    static constexpr int kXRow = kXTma ? 128 : XFragF32::kRowBytes;
-    static constexpr int kXUnit = kXRows * kXRow;
-    static constexpr int kSUnit = kGroupCols * (int)sizeof(ST);
+    static constexpr int kWBytes = kUPS * kGroupStrips * kCB;  // weights of a full group
+    static constexpr bool kXTma = sizeof(AT) == 2;            // 16-bit activations: one TMA box per block
+    static constexpr int kXElt = (int)sizeof(AT);
+    static constexpr int kXRowBytes = kBlockK * kXElt;             // activation bytes per row and block
+    static constexpr int kXRow = kXTma ? 128 : kXRowBytes + 16;   // 128B-swizzled rows / padded rows
+    static constexpr int kXUnit = kMaxRows * kXRow;
+    static constexpr int kSElt = (int)sizeof(ST);
+    static constexpr int kSUnit = kGroupCols * kSElt;
     static constexpr int kBUnit = kBias ? kGroupCols * 4 : 0;
-    static constexpr int kX = kW;
+    static constexpr int kX = align_up(kWBytes, 1024);  // swizzled TMA destination: 1024-byte aligned
     static constexpr int kS = kX + kUPS * kXUnit;
     static constexpr int kB = kS + kUPS * kSUnit;
-    static constexpr int kBytes = align_up(kB + kUPS * kBUnit, 128);
-    static constexpr int kStages = clampi(kRingBudget / kBytes, 2, 8);
-    static constexpr int kPair = 2 * 8 * MT * 32 * 16;  // two buffers of half 1's sums (float4 per lane)
-    static constexpr int kSmem = kStages * kBytes + kPair + 128 /* base alignment slack */ + 2 * kStages * 8 + 16;
+    static constexpr int kBytes = align_up(kB + kUPS * kBUnit, 1024);
+    static constexpr int kStages = 4;
+    static constexpr int kSmem = kStages * kBytes + 1024 /* base alignment slack */ + 2 * kStages * 8;
 };
 
-struct alignas(16) DecodeParams {
+struct alignas(64) DecodeParams {
+    CUtensorMap x_map;  // 16-bit activations [M][K]: box 64 x 16, 128B swizzle, OOB rows read zero
     const void* A;
     const uint8_t* W;
     const void* S;
     const float* bias;
     void* C;
-    unsigned* err;       // device error word
-    unsigned* counters;  // [NSG] arrivals per strip group (workspace; zero between calls)
-    float4* partials;    // [G][2][kNC][MT * 32] fp32 partial fragments (workspace)
+    unsigned* err;  // device error word
     int M, N, K, group;
+    int cs;             // CTAs per strip group (cluster size)
     int early_weights;  // stream weights/scales before the previous kernel finishes
 };
 
-// One stage: k-blocks [kb, kb + n) of strip group sg.
-struct Span {
-    int sg, kb, n;
-};
-
-// The stage sequence of a unit range, identical for the producer and the
-// consumers (incremental: no 64-bit division per stage).
-struct Walker {
-    int sg, kb, left, KB, ups;
-    __device__ __forceinline__ Walker(long long u, long long end, int KB_, int ups_)
-        : sg((int)(u / KB_)), kb((int)(u % KB_)), left((int)(end - u)), KB(KB_), ups(ups_) {}
-    __device__ __forceinline__ bool next(Span& s) {
-        if (left <= 0) return false;
-        int n = KB - kb < ups ? KB - kb : ups;
-        if (n > left) n = left;
-        s.sg = sg;
-        s.kb = kb;
-        s.n = n;
-        left -= n;
-        kb += n;
-        if (kb == KB) {
-            kb = 0;
-            ++sg;
-        }
-        return true;
+// fp16 / bf16 activations: the 16 k (4 MMA steps) of one token row for this lane.
+template <typename AT>
+struct XFrag {
+    uint4 a, b;
+    // TMA tile: row `r`, 16-byte chunks c at ((c ^ (r & 7)) << 4) (128B swizzle).
+    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t) {
+        const uint8_t* row = tile + r * 128;
+        a = *reinterpret_cast<const uint4*>(row + (((2 * t) ^ (r & 7)) << 4));
+        b = *reinterpret_cast<const uint4*>(row + (((2 * t + 1) ^ (r & 7)) << 4));
+    }
+    __device__ __forceinline__ uint32_t b0(int step) const {
+        return step == 0 ? a.x : step == 1 ? a.z : step == 2 ? b.x : b.z;
+    }
+    __device__ __forceinline__ uint32_t b1(int step) const {
+        return step == 0 ? a.y : step == 1 ? a.w : step == 2 ? b.y : b.w;
     }
 };
 
-__device__ __forceinline__ long long range_begin(long long U, int G, int c) { return U * c / G; }
+// fp32 activations (padded rows): x = hi + lo with hi = fp16(x), lo = fp16(x - hi);
+// two MMAs per step keep the product accurate to ~2^-22 relative.
+struct XFragF32 {
+    uint32_t hi[8], lo[8];
+    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t) {
+        const uint8_t* sp = tile + r * (kBlockK * 4 + 16) + 16 * t * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint4 q = *reinterpret_cast<const uint4*>(sp + 16 * i);
+            float4 v = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z),
+                                   __uint_as_float(q.w));
+            __half2 h0 = __floats2half2_rn(v.x, v.y);
+            __half2 h1 = __floats2half2_rn(v.z, v.w);
+            float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+            __half2 l0 = __floats2half2_rn(v.x - f0.x, v.y - f0.y);
+            __half2 l1 = __floats2half2_rn(v.z - f1.x, v.w - f1.y);
+            hi[2 * i] = *reinterpret_cast<uint32_t*>(&h0);
+            hi[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h1);
+            lo[2 * i] = *reinterpret_cast<uint32_t*>(&l0);
+            lo[2 * i + 1] = *reinterpret_cast<uint32_t*>(&l1);
+        }
+    }
+};
 
-// The CTA whose range holds unit u.
-__device__ __forceinline__ int cta_of(long long u, long long U, int G) {
-    int c = (int)((u * G) / U);
-    while (c + 1 < G && range_begin(U, G, c + 1) <= u) ++c;
-    while (c > 0 && range_begin(U, G, c) > u) --c;
-    return c;
+template <typename AT>
+struct ComputeType {
+    static constexpr bool bf16 = false;
+};
+template <>
+struct ComputeType<__nv_bfloat16> {
+    static constexpr bool bf16 = true;
+};
+
+// A fragments (4 regs) of each of the four m16n8k16 steps from a lane's chunk words.
+// kRaw: raw "magic + code" values (see hq_common.cuh); otherwise exact q (or u).
+template <int WBITS, bool kBF16, bool kUnsigned, bool kRaw>
+struct WFrag {
+    uint32_t r[4][4];  // [step][reg]
+    __device__ __forceinline__ void expand(uint32_t w, uint32_t (&o)[4]) {
+        if constexpr (kRaw) {
+            if constexpr (kBF16)
+                raw_u4_bf16(w, o);
+            else
+                raw_u4_f16(w, o);
+        } else {
+            if constexpr (kBF16)
+                dequant_u4_bf16<kUnsigned>(w, o);
+            else
+                dequant_u4_f16<kUnsigned>(w, o);
+        }
+    }
+    __device__ __forceinline__ void build(uint4 w) {
+        if constexpr (WBITS == 4) {
+            uint32_t g0[4], g8[4];
+            // words: x = row g k0..7, y = row g k8..15, z = row g+8 k0..7, w = row g+8 k8..15
+            expand(w.x, g0);
+            expand(w.z, g8);
+            r[0][0] = g0[0]; r[0][1] = g8[0]; r[0][2] = g0[1]; r[0][3] = g8[1];
+            r[1][0] = g0[2]; r[1][1] = g8[2]; r[1][2] = g0[3]; r[1][3] = g8[3];
+            expand(w.y, g0);
+            expand(w.w, g8);
+            r[2][0] = g0[0]; r[2][1] = g8[0]; r[2][2] = g0[1]; r[2][3] = g8[1];
+            r[3][0] = g0[2]; r[3][1] = g8[2]; r[3][2] = g0[3]; r[3][3] = g8[3];
+        } else {
+            // words: x = row g k0..15, y = row g+8 k0..15
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                if constexpr (kRaw) {
+                    r[s][0] = raw_t2_pair<kBF16>(w.x, 2 * s);
+                    r[s][1] = raw_t2_pair<kBF16>(w.y, 2 * s);
+                    r[s][2] = raw_t2_pair<kBF16>(w.x, 2 * s + 1);
+                    r[s][3] = raw_t2_pair<kBF16>(w.y, 2 * s + 1);
+                } else {
+                    r[s][0] = dequant_t2_pair<kBF16>(w.x, 2 * s);
+                    r[s][1] = dequant_t2_pair<kBF16>(w.y, 2 * s);
+                    r[s][2] = dequant_t2_pair<kBF16>(w.x, 2 * s + 1);
+                    r[s][3] = dequant_t2_pair<kBF16>(w.y, 2 * s + 1);
+                }
+            }
+        }
+    }
+};
+
+// Raw-value correction: the A constant whose MMA with step s's activation
+// fragment gives -(M + offset) * sum(x) (fp16 int4: odd steps see x/16 and
+// weights 1024 + 16u, hence 1152 = 72 * 16).
+template <int WBITS, bool kBF16>
+__device__ __forceinline__ uint32_t raw_corr_const(int step) {
+    if constexpr (WBITS == 4) {
+        if constexpr (kBF16) return 0xC308C308u;                   // -136
+        else return (step & 1) ? 0xE480E480u : 0xE408E408u;       // -1152 / -1032
+    } else {
+        return kBF16 ? 0xC301C301u : 0xE401E401u;                  // -129 / -1025
+    }
+}
+
+template <typename ST>
+__device__ __forceinline__ float lds_scale(const uint8_t* sp) {
+    return to_f32(*reinterpret_cast<const ST*>(sp));
 }
 
 template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using L = Ring<WBITS, MT, AT, ST, kBias>;
+__global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const __grid_constant__ DecodeParams p) {
+    using L = Stage<WBITS, AT, ST, kBias>;
     constexpr bool kSplit = std::is_same<AT, float>::value;
     constexpr bool kBF16 = ComputeType<AT>::bf16;  // float activations compute in fp16
     constexpr int kCB = L::kCB;
     constexpr int kLaneBytes = kCB / 32;
     constexpr int kStages = L::kStages;
-    constexpr int kUPS = L::kUPS;
+    // Raw path (M <= 8 with fp16/bf16 activations, symmetric weights): MMA on
+    // magic + code, offset removed by the per-block correction that seeds the
+    // accumulator.  M > 8 subtracts on the FMA pipe instead, sparing the
+    // legacy MMA rate which binds there.
+    constexpr bool kRaw = false;
+    constexpr bool kHiScale = kRaw && WBITS == 4 && !kBF16;  // fp16 int4: x/16 on odd steps
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* ring = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
-    float4* pair_buf = reinterpret_cast<float4*>(ring + kStages * L::kBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * L::kBytes + L::kPair);
+    uint8_t* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * L::kBytes);
     uint64_t* empty = full + kStages;
-    volatile int* s_last = reinterpret_cast<volatile int*>(empty + kStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom geo(p.K, p.N, WBITS);
     const int KB = geo.KB;
-    const long long U = geo.units();
-    const int G = (int)gridDim.x, c = (int)blockIdx.x;
-    const long long u_begin = range_begin(U, G, c), u_end = range_begin(U, G, c + 1);
+    const int cs = p.cs;
+    const int sg = blockIdx.x / cs;
+    const int rank = cs > 1 ? (int)cluster_ctarank() : 0;
+    const int width = geo.width(sg);
+    const int kb_begin = rank * KB / cs, kb_end = (rank + 1) * KB / cs;
+    const int n_units = kb_end - kb_begin;
+    const int n_iters = (n_units + kUPS - 1) / kUPS;
+    const uint32_t unit_bytes = (uint32_t)width * kCB;  // one k-block of this strip group
+    const size_t off0 = geo.unit_offset((long long)sg * KB + kb_begin);
     const int upg = p.group / kBlockK;  // k-blocks per scale group
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1 + 32 * kProducerWarps);  // the code copy's expect-tx + one cp.async arrival per producer lane
-            mbar_init(&empty[i], kNC);
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kConsumerWarps);
         }
         fence_mbarrier_init();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -188,117 +246,259 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     __syncthreads();
 
-    if (warp >= kProducerWarp) {
-        // --------------------------------------------------------- producers
-        // Warp kProducerWarp issues the stage's codes as one bulk copy; the small
-        // operands (activation rows, scale and bias rows) go as 16-byte cp.async
-        // spread over both producer warps, each lane then arriving once they land.
-        const int pl = (warp - kProducerWarp) * 32 + lane;
-        constexpr int kPL = 32 * kProducerWarps;
+    float acc[kStripsPerWarp][MT][4];
+#pragma unroll
+    for (int j = 0; j < kStripsPerWarp; ++j)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][m][i] = 0.f;
+
+    if (warp == kConsumerWarps) {
+        // ---------------------------------------------------------- producer
         const uint64_t pol = l2_policy_evict_first();
         const uint8_t* Ab = reinterpret_cast<const uint8_t*>(p.A);
         const uint8_t* Sb = reinterpret_cast<const uint8_t*>(p.S);
         const uint8_t* Bb = reinterpret_cast<const uint8_t*>(p.bias);
-        const int xrows = p.M < L::kXRows ? p.M : L::kXRows;  // rows >= M feed only unstored MMA columns
-        auto stage_ptr = [&](int it) { return ring + (it % kStages) * L::kBytes; };
-        // Codes, scales and biases of stage `it` (no earlier kernel writes them).
-        auto issue_w = [&](int it, const Span& d) {
+        const uint32_t cols = (uint32_t)width * kStripCols;
+        const uint32_t s_bytes = cols * L::kSElt, b_bytes = kBias ? cols * 4 : 0;
+        const uint32_t x_bytes = L::kXTma ? (uint32_t)L::kXUnit : (uint32_t)(p.M * L::kXRowBytes);
+        // Activation tiles of stage `it` (the part that depends on the previous kernel).
+        auto issue_x = [&](int it) {
             const int slot = it % kStages;
-            uint8_t* st = stage_ptr(it);
-            const int width = geo.width(d.sg);
-            const int s_chunks = width * kStripCols * (int)sizeof(ST) / 16;
-            const int b_chunks = kBias ? width * kStripCols * 4 / 16 : 0;
-            const uint32_t wbytes = (uint32_t)d.n * (uint32_t)width * kCB;
-            if (pl == 0) {
-                mbar_arrive_expect_tx(&full[slot], wbytes);
-                bulk_g2s_hint(st, p.W + geo.unit_offset((long long)d.sg * KB + d.kb), wbytes, &full[slot], pol);
-            }
-            // one scale (and bias) row per k-block: [group][the group's columns]
-            for (int i = pl; i < d.n * (s_chunks + b_chunks); i += kPL) {
-                const int r = i / (s_chunks + b_chunks), cc = i - r * (s_chunks + b_chunks);
-                const size_t off = (size_t)((d.kb + r) / upg) * p.N + (size_t)d.sg * kGroupCols;
-                if (cc < s_chunks)
-                    cp_async16(st + L::kS + r * L::kSUnit + 16 * cc, Sb + off * sizeof(ST) + 16 * cc);
-                else if constexpr (kBias)
-                    cp_async16(st + L::kB + r * L::kBUnit + 16 * (cc - s_chunks), Bb + off * 4 + 16 * (cc - s_chunks));
+            uint8_t* st = ring + slot * L::kBytes;
+            const int nu = min(kUPS, n_units - it * kUPS);
+            if constexpr (L::kXTma) {
+                if (lane == 0)
+                    for (int ul = 0; ul < nu; ++ul)
+                        tma_load_2d(st + L::kX + ul * L::kXUnit, &p.x_map, (kb_begin + it * kUPS + ul) * kBlockK, 0,
+                                    &full[slot]);
+            } else {
+#pragma unroll
+                for (int ul = 0; ul < kUPS; ++ul) {
+                    if (ul < nu && lane < p.M) {
+                        const int kb = kb_begin + it * kUPS + ul;
+                        bulk_g2s(st + L::kX + ul * L::kXUnit + lane * L::kXRow,
+                                 Ab + ((size_t)lane * p.K + (size_t)kb * kBlockK) * L::kXElt, L::kXRowBytes,
+                                 &full[slot]);
+                    }
+                }
             }
         };
-        // Activation rows of stage `it` (may depend on the previous kernel), then
-        // this lane's arrival once its copies of the stage have landed.
-        auto issue_x = [&](int it, const Span& d) {
+        const int early = p.early_weights ? min(kStages, n_iters) : 0;
+        if (!early) pdl_wait();
+        int issued = 0;
+        for (int it = 0; it < n_iters; ++it) {
             const int slot = it % kStages;
-            uint8_t* st = stage_ptr(it);
-            constexpr int kRowChunks = kBlockK * (int)sizeof(AT) / 16;  // 16-byte pieces of one row of one k-block
-            const int per_kb = xrows * kRowChunks;
-            for (int i = pl; i < d.n * per_kb; i += kPL) {
-                const int u = i / per_kb, rem = i - u * per_kb, r = rem / kRowChunks, cc = rem - r * kRowChunks;
-                const uint8_t* src = Ab + ((size_t)r * p.K + (size_t)(d.kb + u) * kBlockK) * sizeof(AT) + 16 * cc;
-                uint8_t* dst = st + L::kX + u * L::kXUnit;
-                if constexpr (L::kXTma)
-                    dst += r * 128 + ((cc ^ (r & 7)) << 4);  // 128-byte rows, XOR-swizzled 16-byte chunks
-                else
-                    dst += r * L::kXRow + 16 * cc;
-                cp_async16(dst, src);
+            const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1u, p.err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const int nu = min(kUPS, n_units - it * kUPS);
+            uint8_t* st = ring + slot * L::kBytes;
+            if (lane == 0) {
+                const uint32_t wbytes = (uint32_t)nu * unit_bytes;
+                mbar_arrive_expect_tx(&full[slot], wbytes + (uint32_t)nu * (x_bytes + s_bytes + b_bytes));
+                bulk_g2s_hint(st, p.W + off0 + (size_t)it * kUPS * unit_bytes, wbytes, &full[slot], pol);
             }
-            cp_async_mbar_arrive(&full[slot]);
-        };
-        Walker wk(u_begin, u_end, KB, kUPS);
-        Span d;
-        Span pend[kStages];
-        int it = 0;
-        // First pass over the ring: every slot is free.  Codes first; activations
-        // once the previous kernel has finished.
-        if (!p.early_weights) pdl_wait();
-        while (it < kStages && wk.next(d)) {
-            issue_w(it, d);
-            if (p.early_weights)
-                pend[it] = d;
-            else
-                issue_x(it, d);
-            ++it;
+            __syncwarp();
+            // scale (and bias) row of each k-block: [group][the 128 columns]
+            if (lane >= 16 && lane < 16 + nu) {
+                const int i = lane - 16;
+                const int gi = (kb_begin + it * kUPS + i) / upg;
+                const size_t off = (size_t)gi * p.N + (size_t)sg * kGroupCols;
+                bulk_g2s(st + L::kS + i * L::kSUnit, Sb + off * L::kSElt, s_bytes, &full[slot]);
+                if constexpr (kBias) bulk_g2s(st + L::kB + i * L::kBUnit, Bb + off * 4, b_bytes, &full[slot]);
+            }
+            if (it >= early) {
+                issue_x(it);
+            } else if (it == early - 1) {
+                // First stages' weights are in flight; now wait for the previous
+                // kernel (which may have produced A) and add their activations.
+                pdl_wait();
+                for (int j = 0; j < early; ++j) issue_x(j);
+            }
+            issued = it + 1;
         }
-        if (p.early_weights) {
+        if (issued < early) {  // timed out before the early stages were completed
             pdl_wait();
-            for (int j = 0; j < it; ++j) issue_x(j, pend[j]);
+            for (int j = 0; j < issued; ++j) issue_x(j);
         }
-        while (wk.next(d)) {
-            const int slot = it % kStages;
-            int w_ok = 1;
-            if (lane == 0) w_ok = mbar_wait(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
-            w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-            if (!w_ok) break;
-            issue_w(it, d);
-            issue_x(it, d);
-            ++it;
-        }
-        // Copies still in flight land before the CTA exits.
+        // Copies still in flight land before the ring is reused or the CTA exits.
         if (lane == 0)
-            for (int j = it - kStages < 0 ? 0 : it - kStages; j < it; ++j)
-                mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1u, p.err);
+            for (int it = issued - kStages < 0 ? 0 : issued - kStages; it < issued; ++it)
+                mbar_wait(&full[it % kStages], (uint32_t)(it / kStages) & 1u, p.err);
         __syncwarp();
-        return;
+    } else {
+        // -------------------------------------------------------- consumers
+        const int g = lane >> 2, t = lane & 3;
+        using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
+        const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
+        // After a timed-out wait the warp stops waiting but keeps the same
+        // control flow (results are garbage, the error word is set): every
+        // thread still reaches the barriers below, so nothing hangs.
+        bool waits_ok = true;
+        for (int it = 0; it < n_iters; ++it) {
+            const int slot = it % kStages;
+            if (waits_ok) waits_ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
+            const int nu = min(kUPS, n_units - it * kUPS);
+            const int kb0 = kb_begin + it * kUPS;
+            // Both blocks of the stage in one scale group: one scale application.
+            const bool same = nu == 2 && (kb0 % upg) != upg - 1;
+            const uint8_t* stage = ring + slot * L::kBytes;
+
+            // Activation fragments (and raw-path corrections) of the stage's blocks.
+            XF xf[kUPS][MT];
+            float corr[kUPS][MT][4];
+            float xs[kUPS][MT][4];
+#pragma unroll
+            for (int u = 0; u < kUPS; ++u) {
+                if (u >= nu) continue;
+                const uint8_t* tile = stage + L::kX + u * L::kXUnit;
+#pragma unroll
+                for (int m = 0; m < MT; ++m) xf[u][m].load(tile, 8 * m + g, t);
+                // Rows >= M are zero (TMA fill) or stale (padded copies); either way
+                // they only feed MMA columns (tokens) that are never stored.
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) corr[u][m][i] = 0.f;
+                if constexpr (kRaw) {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        if constexpr (kHiScale) {
+                            const uint32_t kSixteenth = 0x2C002C00u;
+                            xf[u][m].a.z = hmul2_bits(xf[u][m].a.z, kSixteenth);
+                            xf[u][m].a.w = hmul2_bits(xf[u][m].a.w, kSixteenth);
+                            xf[u][m].b.z = hmul2_bits(xf[u][m].b.z, kSixteenth);
+                            xf[u][m].b.w = hmul2_bits(xf[u][m].b.w, kSixteenth);
+                        }
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            const uint32_t c = raw_corr_const<WBITS, kBF16>(s);
+                            const uint32_t ca[4] = {c, c, c, c};
+                            mma_16816<kBF16>(corr[u][m], ca, xf[u][m].b0(s), xf[u][m].b1(s));
+                        }
+                    }
+                }
+                if constexpr (kBias) {
+                    const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) xs[u][m][i] = 0.f;
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            if constexpr (kSplit) {
+                                mma_16816<false>(xs[u][m], ones, xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                mma_16816<false>(xs[u][m], ones, xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
+                            } else {
+                                mma_16816<kBF16>(xs[u][m], ones, xf[u][m].b0(s), xf[u][m].b1(s));
+                            }
+                        }
+                    }
+                }
+            }
+
+#pragma unroll
+            for (int j = 0; j < kStripsPerWarp; ++j) {
+                const int sl = kStripsPerWarp * warp + j;
+                if (sl >= width) continue;
+                const int nl = sl * kStripCols + g;
+                float tacc[kUPS][MT][4];  // per-block partial sums (independent MMA chains)
+#pragma unroll
+                for (int u = 0; u < kUPS; ++u) {
+                    if (u >= nu) continue;
+                    const uint8_t* wp = stage + u * unit_bytes + sl * kCB + lane * kLaneBytes;
+                    uint4 wv;
+                    if constexpr (WBITS == 4) {
+                        wv = *reinterpret_cast<const uint4*>(wp);
+                    } else {
+                        const uint2 v = *reinterpret_cast<const uint2*>(wp);
+                        wv = make_uint4(v.x, v.y, 0, 0);
+                    }
+                    WFrag<WBITS, kBF16, kBias, kRaw> wf;
+                    wf.build(wv);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        if constexpr (kSplit) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) tacc[u][m][i] = 0.f;
+#pragma unroll
+                            for (int s = 0; s < 4; ++s) {
+                                mma_16816<false>(tacc[u][m], wf.r[s], xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                mma_16816<false>(tacc[u][m], wf.r[s], xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
+                            }
+                        } else {
+                            mma_16816_c<kBF16>(tacc[u][m], wf.r[0], xf[u][m].b0(0), xf[u][m].b1(0), corr[u][m]);
+#pragma unroll
+                            for (int s = 1; s < 4; ++s)
+                                mma_16816<kBF16>(tacc[u][m], wf.r[s], xf[u][m].b0(s), xf[u][m].b1(s));
+                        }
+                    }
+                }
+                // Apply the group scales (and the bias term of the reference form).
+                const uint8_t* s0p = stage + L::kS;
+                const float sa0 = lds_scale<ST>(s0p + nl * L::kSElt);
+                const float sa1 = lds_scale<ST>(s0p + (nl + 8) * L::kSElt);
+                if constexpr (kBias) {
+#pragma unroll
+                    for (int u = 0; u < kUPS; ++u) {
+                        if (u >= nu) continue;
+                        const float s0 = u ? lds_scale<ST>(s0p + L::kSUnit + nl * L::kSElt) : sa0;
+                        const float s1 = u ? lds_scale<ST>(s0p + L::kSUnit + (nl + 8) * L::kSElt) : sa1;
+                        const uint8_t* bp = stage + L::kB + u * L::kBUnit;
+                        const float b0 = lds_scale<float>(bp + nl * 4), b1 = lds_scale<float>(bp + (nl + 8) * 4);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            acc[j][m][0] += tacc[u][m][0] * s0 + xs[u][m][0] * b0;
+                            acc[j][m][1] += tacc[u][m][1] * s0 + xs[u][m][1] * b0;
+                            acc[j][m][2] += tacc[u][m][2] * s1 + xs[u][m][2] * b1;
+                            acc[j][m][3] += tacc[u][m][3] * s1 + xs[u][m][3] * b1;
+                        }
+                    }
+                } else if (same) {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        acc[j][m][0] = fmaf(tacc[0][m][0] + tacc[1][m][0], sa0, acc[j][m][0]);
+                        acc[j][m][1] = fmaf(tacc[0][m][1] + tacc[1][m][1], sa0, acc[j][m][1]);
+                        acc[j][m][2] = fmaf(tacc[0][m][2] + tacc[1][m][2], sa1, acc[j][m][2]);
+                        acc[j][m][3] = fmaf(tacc[0][m][3] + tacc[1][m][3], sa1, acc[j][m][3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        acc[j][m][0] = fmaf(tacc[0][m][0], sa0, acc[j][m][0]);
+                        acc[j][m][1] = fmaf(tacc[0][m][1], sa0, acc[j][m][1]);
+                        acc[j][m][2] = fmaf(tacc[0][m][2], sa1, acc[j][m][2]);
+                        acc[j][m][3] = fmaf(tacc[0][m][3], sa1, acc[j][m][3]);
+                    }
+                    if (nu == 2) {
+                        const float sb0 = lds_scale<ST>(s0p + L::kSUnit + nl * L::kSElt);
+                        const float sb1 = lds_scale<ST>(s0p + L::kSUnit + (nl + 8) * L::kSElt);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            acc[j][m][0] = fmaf(tacc[1][m][0], sb0, acc[j][m][0]);
+                            acc[j][m][1] = fmaf(tacc[1][m][1], sb0, acc[j][m][1]);
+                            acc[j][m][2] = fmaf(tacc[1][m][2], sb1, acc[j][m][2]);
+                            acc[j][m][3] = fmaf(tacc[1][m][3], sb1, acc[j][m][3]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
     }
 
-    // ------------------------------------------------------------ consumers
-    // Two warps per strip: half 0 takes the first half of every stage's
-    // k-blocks, half 1 the second; their sums meet in shared memory when a
-    // strip group is done.
-    pdl_wait();
-    const int g = lane >> 2, t = lane & 3;
-    const int sl = warp & 7, half = warp >> 3;
-    using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
-    const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
+    // ------------------------------------------------------------- epilogue
     OT* C = reinterpret_cast<OT*>(p.C);
-
-    float acc[MT][4];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[m][i] = 0.f;
-
-    auto store_frag = [&](int sg, int m, float4 v) {
-        const int n = sg * kGroupCols + sl * kStripCols + g;
-        const int tok = 8 * m + 2 * t;
+    // Store a float4 of the fragment (strip sl, token tile m, lane) to C.
+    auto store_frag = [&](int sl, int m, int ln, float4 v) {
+        if (sl >= width) return;
+        const int n = sg * kGroupCols + sl * kStripCols + (ln >> 2);
+        const int tok = 8 * m + 2 * (ln & 3);
         if (tok < p.M) {
             C[(size_t)tok * p.N + n] = from_f32<OT>(v.x);
             C[(size_t)tok * p.N + n + 8] = from_f32<OT>(v.z);
@@ -308,217 +508,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             C[(size_t)(tok + 1) * p.N + n + 8] = from_f32<OT>(v.w);
         }
     };
-
-    // A batch of up to kBatch k-blocks (from k-block u0 of the stage) of this
-    // warp's strip: all code and scale loads first, then independent MMA chains
-    // per k-block (so the loads, the dequant and the tensor-core latencies of
-    // different k-blocks overlap), then the scales.  kFull (a whole batch, the
-    // common case) is straight-line code; otherwise k-blocks u >= n are skipped
-    // by warp-uniform branches.
-    auto consume_batch = [&](const uint8_t* stage, int u0, int width, int n, auto full_tag) {
-        constexpr bool kFull = decltype(full_tag)::value;
-        constexpr int kUPS = kBatch;
-        const uint32_t unit_bytes = (uint32_t)width * kCB;
-        const int nl = sl * kStripCols + g;  // column within the group
-        uint4 wv[kUPS];
-        float sc0[kUPS], sc1[kUPS];
+    if (cs == 1) {
+        if (warp < kConsumerWarps) {
 #pragma unroll
-        for (int u = 0; u < kUPS; ++u) {
-            const bool on = kFull || u < n;
-            const uint8_t* wp = stage + (u0 + u) * unit_bytes + sl * kCB + lane * kLaneBytes;
-            if constexpr (WBITS == 4) {
-                wv[u] = on ? *reinterpret_cast<const uint4*>(wp) : make_uint4(0u, 0u, 0u, 0u);
-            } else {
-                const uint2 v = on ? *reinterpret_cast<const uint2*>(wp) : make_uint2(0u, 0u);
-                wv[u] = make_uint4(v.x, v.y, 0u, 0u);
-            }
-            const uint8_t* sp = stage + L::kS + (u0 + u) * L::kSUnit;
-            sc0[u] = on ? lds_scale<ST>(sp + nl * sizeof(ST)) : 0.f;
-            sc1[u] = on ? lds_scale<ST>(sp + (nl + 8) * sizeof(ST)) : 0.f;
-        }
-        float tacc[kUPS][MT][4];
-        float xs[kUPS][MT][4];
-#pragma unroll
-        for (int u = 0; u < kUPS; ++u) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) tacc[u][m][i] = xs[u][m][i] = 0.f;
-            if (!kFull && u >= n) continue;
-            const uint8_t* tile = stage + L::kX + (u0 + u) * L::kXUnit;
-            WFrag<WBITS, kBF16, kBias> wf;
-            wf.build(wv[u]);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                XF xf;
-                xf.load(tile, 8 * m + g, t);
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    if constexpr (kSplit) {
-                        mma_16816<false>(tacc[u][m], wf.r[s], xf.hi[2 * s], xf.hi[2 * s + 1]);
-                        mma_16816<false>(tacc[u][m], wf.r[s], xf.lo[2 * s], xf.lo[2 * s + 1]);
-                    } else {
-                        mma_16816<kBF16>(tacc[u][m], wf.r[s], xf.b0(s), xf.b1(s));
-                    }
-                }
-                if constexpr (kBias) {
-                    // Row sums of the activations (a ones A operand): the bias term b * sum(x).
-                    const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        if constexpr (kSplit) {
-                            mma_16816<false>(xs[u][m], ones, xf.hi[2 * s], xf.hi[2 * s + 1]);
-                            mma_16816<false>(xs[u][m], ones, xf.lo[2 * s], xf.lo[2 * s + 1]);
-                        } else {
-                            mma_16816<kBF16>(xs[u][m], ones, xf.b0(s), xf.b1(s));
-                        }
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kUPS; ++u) {
-            if (!kFull && u >= n) continue;
-            float b0 = 0.f, b1 = 0.f;
-            if constexpr (kBias) {
-                const uint8_t* bp = stage + L::kB + (u0 + u) * L::kBUnit;
-                b0 = lds_scale<float>(bp + nl * 4);
-                b1 = lds_scale<float>(bp + (nl + 8) * 4);
-            }
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                acc[m][0] = fmaf(tacc[u][m][0], sc0[u], acc[m][0]);
-                acc[m][1] = fmaf(tacc[u][m][1], sc0[u], acc[m][1]);
-                acc[m][2] = fmaf(tacc[u][m][2], sc1[u], acc[m][2]);
-                acc[m][3] = fmaf(tacc[u][m][3], sc1[u], acc[m][3]);
-                if constexpr (kBias) {
-                    acc[m][0] = fmaf(xs[u][m][0], b0, acc[m][0]);
-                    acc[m][1] = fmaf(xs[u][m][1], b0, acc[m][1]);
-                    acc[m][2] = fmaf(xs[u][m][2], b1, acc[m][2]);
-                    acc[m][3] = fmaf(xs[u][m][3], b1, acc[m][3]);
-                }
-            }
-        }
-    };
-
-    const int first_sg = (int)(u_begin / KB);
-    int pend_sg[2] = {-1, -1};  // strip groups handed to the fixup, by slot
-    int nflush = 0;
-    // Strip group `sg` is done for this CTA: half 1 hands its sums to half 0,
-    // which stores the group or, when other CTAs share it, writes the partial
-    // and lets thread 0 count the arrival (the last arriver sums after the loop).
-    auto flush_group = [&](int sg) {
-        float4* xch = pair_buf + ((nflush & 1) * 8 + sl) * (MT * 32);
-        ++nflush;
-        if (half == 1) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) xch[m * 32 + lane] = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
-        }
-        named_bar_sync(kPairBar, kNC * 32);
-        if (half == 0) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const float4 v = xch[m * 32 + lane];
-                acc[m][0] += v.x;
-                acc[m][1] += v.y;
-                acc[m][2] += v.z;
-                acc[m][3] += v.w;
-            }
-            const int width = geo.width(sg);
-            const long long g0 = (long long)sg * KB, g1 = g0 + KB;
-            if (g0 >= u_begin && g1 <= u_end) {
-                if (sl < width)
-#pragma unroll
-                    for (int m = 0; m < MT; ++m)
-                        store_frag(sg, m, make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]));
-            } else {
-                const int slot = sg == first_sg ? 0 : 1;
-                float4* mine = p.partials + (((size_t)c * 2 + slot) * 8 + sl) * (MT * 32);
+            for (int j = 0; j < kStripsPerWarp; ++j)
 #pragma unroll
                 for (int m = 0; m < MT; ++m)
-                    mine[m * 32 + lane] = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
-                named_bar_sync(kHalfBar, 8 * 32);
-                if (threadIdx.x == 0) {
-                    __threadfence();  // cumulative: orders every half-0 partial before the arrival
-                    const int c_first = cta_of(g0, U, G), c_last = cta_of(g1 - 1, U, G);
-                    const unsigned old = atomicAdd(&p.counters[sg], 1u);
-                    s_last[slot] = old == (unsigned)(c_last - c_first);
-                }
-                pend_sg[slot] = sg;
-            }
+                    store_frag(kStripsPerWarp * warp + j, m, lane,
+                               make_float4(acc[j][m][0], acc[j][m][1], acc[j][m][2], acc[j][m][3]));
         }
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[m][i] = 0.f;
-    };
-
-    // After a timed-out wait the warp stops waiting but keeps the same control
-    // flow (results are garbage, the error word is set): every thread still
-    // reaches the barriers, so nothing hangs.
-    bool waits_ok = true;
-    Walker wk(u_begin, u_end, KB, kUPS);
-    Span d;
-    int it = 0, cur = -1;
-    constexpr int kHalfUnits = kUPS / 2;
-    while (wk.next(d)) {
-        if (d.sg != cur) {
-            if (cur >= 0) flush_group(cur);
-            cur = d.sg;
-        }
-        const int slot = it % kStages;
-        if (waits_ok) waits_ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
-        const uint8_t* stage = ring + slot * L::kBytes;
-        const int width = geo.width(d.sg);
-        if (sl < width) {
-#pragma unroll
-            for (int b = 0; b < kHalfUnits; b += kBatch) {
-                const int u0 = half * kHalfUnits + b;
-                const int nb = d.n - u0;
-                if (nb >= kBatch)
-                    consume_batch(stage, u0, width, kBatch, std::true_type{});
-                else if (nb > 0)
-                    consume_batch(stage, u0, width, nb, std::false_type{});
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        ++it;
+        return;
     }
-    if (cur >= 0) flush_group(cur);
-
-    // Strip groups shared with other CTAs that this CTA reached last: sum every
-    // sharer's partial in CTA order, store, and reset the group's counter.
-    if (half == 0) {
-        named_bar_sync(kHalfBar, 8 * 32);  // thread 0's arrival results are visible
+    // Cluster split-K: partial fragments to this CTA's shared memory (the ring,
+    // idle now: every issued copy has landed and been consumed), cluster
+    // barrier, then CTA `rank` reduces its 1/cs share over all cs CTAs in rank
+    // order and writes C; a second barrier keeps every CTA's shared memory
+    // alive until all remote reads are done.
+    constexpr int kFrags = kConsumerWarps * kStripsPerWarp * MT * 32;  // float4 per CTA
+    const uint32_t red = smem_u32(ring);
+    __syncthreads();
+    if (warp < kConsumerWarps) {
 #pragma unroll
-        for (int slot = 0; slot < 2; ++slot) {
-            const int sg = pend_sg[slot];
-            if (sg < 0 || !s_last[slot]) continue;
-            __threadfence();
-            const long long g0 = (long long)sg * KB, g1 = g0 + KB;
-            const int c_first = cta_of(g0, U, G), c_last = cta_of(g1 - 1, U, G);
-            float4 sum[MT];
+        for (int j = 0; j < kStripsPerWarp; ++j)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) sum[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = c_first; q <= c_last; ++q) {
-                const int qslot = (int)(range_begin(U, G, q) / KB) == sg ? 0 : 1;
-                const float4* src = p.partials + (((size_t)q * 2 + qslot) * 8 + sl) * (MT * 32);
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    const float4 v = __ldcg(src + m * 32 + lane);
-                    sum[m].x += v.x;
-                    sum[m].y += v.y;
-                    sum[m].z += v.z;
-                    sum[m].w += v.w;
-                }
+            for (int m = 0; m < MT; ++m) {
+                const int i = ((warp * kStripsPerWarp + j) * MT + m) * 32 + lane;
+                sts_f4(red + 16 * i, make_float4(acc[j][m][0], acc[j][m][1], acc[j][m][2], acc[j][m][3]));
             }
-            if (sl < geo.width(sg))
-#pragma unroll
-                for (int m = 0; m < MT; ++m) store_frag(sg, m, sum[m]);
-            if (threadIdx.x == 0) p.counters[sg] = 0u;
-        }
     }
+    cluster_sync();
+    const int share = (kFrags + cs - 1) / cs;  // cs need not divide kFrags
+    for (int i = rank * share + (int)threadIdx.x; i < min(kFrags, (rank + 1) * share); i += kThreads) {
+        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < cs; ++q) {
+            const float4 v = ld_dsmem_f4(mapa_shared(red + 16 * i, (uint32_t)q));
+            s4.x += v.x;
+            s4.y += v.y;
+            s4.z += v.z;
+            s4.w += v.w;
+        }
+        const int ln = i & 31, rest = i >> 5;
+        const int m = rest % MT, wj = rest / MT;
+        store_frag(wj, m, ln, s4);  // wj = warp * 2 + j = strip index
+    }
+    cluster_sync();
 }
 
 using KernelFn = void (*)(DecodeParams);
@@ -527,13 +560,12 @@ struct KernelInfo {
     KernelFn fn = nullptr;
     int smem = 0;
     bool x_tma = false;
-    int x_rows = 0;
 };
 
 template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
 KernelInfo kernel_info() {
-    using L = Ring<WBITS, MT, AT, ST, kBias>;
-    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias>, L::kSmem, L::kXTma, L::kXRows};
+    using L = Stage<WBITS, AT, ST, kBias>;
+    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias>, L::kSmem, L::kXTma};
 }
 
 // Output dtype: the activation's own 16-bit type or f32 (f32 activations: f32 out).
@@ -580,15 +612,28 @@ KernelInfo select_kernel(const GemmArgs& a) {
     return MT == 1 ? pick<2, 1>(a) : pick<2, 2>(a);
 }
 
-int grid_ctas(int N, int K, int wbits, int dev) {
-    const long long U = TileGeom(K, N, wbits).units();
-    const long long G = (long long)device_info(dev).sm_count * kCtasPerSm;
-    return (int)(U < G ? U : G);
-}
-
-size_t counters_bytes(int N) {
-    const size_t nsg = (size_t)((N / kStripCols + kGroupStrips - 1) / kGroupStrips);
-    return (nsg * 4 + 255) & ~(size_t)255;
+// CTAs per strip group, from {1, 2, 4, 8, 10, 12} (<= KB): the cs minimising
+// resident waves x k-blocks per CTA plus a reduction cost that grows with cs,
+// using the measured cluster occupancy of this kernel.  Narrow layers (N = 5120:
+// 40 strip groups) need clusters of more than 8 CTAs to put enough bytes in
+// flight per SM; larger clusters (14, 16) measured slower on B200.
+int cluster_size(const void* fn, int smem, int N, int K, int wbits, int dev) {
+    const TileGeom geo(K, N, wbits);
+    static const int kCandidates[] = {1, 2, 4, 8, 10, 12};
+    int best = 1;
+    long long best_cost = -1;
+    for (int cs : kCandidates) {
+        if (cs > geo.KB) break;
+        const int clusters = max_active_clusters(fn, kThreads, smem, cs, dev);
+        if (clusters <= 0) continue;
+        const long long waves = (geo.NSG + clusters - 1) / clusters;
+        const long long cost = waves * ((geo.KB + cs - 1) / cs) * 8 + 8 * cs;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = cs;
+        }
+    }
+    return best;
 }
 
 bool g_early_weights = true;
@@ -599,18 +644,10 @@ void set_decode_launch_overlap(bool on) { g_early_weights = on; }
 
 bool decode_supported(const GemmArgs& a) { return select_kernel(a).fn != nullptr; }
 
-// Arrival counters (one per strip group) followed by the partial tiles of the
-// split strip groups: two per CTA, eight warps x 2 token tiles x 32 lanes x 16 B.
-size_t decode_counters_bytes(int N) { return counters_bytes(N); }
-
-size_t decode_split_bytes(int N, int K, int wbits, int dev) {
-    const size_t G = (size_t)grid_ctas(N, K, wbits, dev);
-    return counters_bytes(N) + G * 2 * kNC * 2 * 32 * sizeof(float4);
-}
-
+// Only the integer-MMA kernel (wide layers) keeps state in the workspace.
 size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev) {
     (void)M;
-    return decode_split_bytes(N, K, wbits, dev) + (wbits == 4 ? decode_i8_extra_bytes(K) : 0);
+    return wbits == 4 ? decode_i8_workspace_bytes(N, K, dev) : 0;
 }
 
 cudaError_t launch_decode(const GemmArgs& a) {
@@ -618,22 +655,31 @@ cudaError_t launch_decode(const GemmArgs& a) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (a.M < 1 || a.M > kMaxRows) return cudaErrorInvalidValue;
-#if HQ_DECODE_I8
-    // int4 codes x 16-bit activations, no bias: the integer tensor-core kernel.
-    if (decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
-#endif
-#if HQ_DECODE_TC_ROUTE
-    // M > 8 on wide layers may run on tcgen05 (its cost does not depend on M).
+    // Wide layers (>= 128 strip groups) at M <= 4 with 16-bit activations stream
+    // faster through the integer-MMA kernel (hq_decode_i8.cu; gate_up 5120 x
+    // 34816: 26.2 us against 28.0 here): its consumer spends ~3x fewer
+    // instructions per byte of codes.  Narrow layers, and M > 4, keep this
+    // kernel, whose cluster split-K has a shorter start-up and tail.
+    if (a.M <= 4 && TileGeom(a.K, a.N, a.wbits).NSG >= 128 && decode_i8_supported(a))
+        return launch_decode_i8(a, g_early_weights);
+    // M > 8 on wide layers runs on tcgen05: the mma.sync kernel needs two token
+    // tiles there and the tensor-memory kernel's cost does not depend on M.
+    // Narrow layers (few strip groups) and M <= 8 stream faster here.
     if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= 48 && decode_tc_supported(a))
         return launch_decode_tc(a, g_early_weights);
-#endif
+    const TileGeom geo(a.K, a.N, a.wbits);
     const KernelInfo ki = select_kernel(a);
     if (!ki.fn) return cudaErrorInvalidValue;
-    if (!a.ws || a.ws_bytes < decode_workspace_bytes(a.M, a.N, a.K, a.wbits, dev)) return cudaErrorInvalidValue;
     e = ensure_smem_attr(reinterpret_cast<const void*>(ki.fn), dev, ki.smem);
     if (e != cudaSuccess) return e;
     DecodeParams p;
     memset(&p, 0, sizeof p);
+    if (ki.x_tma) {
+        // [M][K] 16-bit activations; a box is 64 k x 16 rows, rows >= M read zero.
+        e = make_tmap_2d(&p.x_map, a.A, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.M,
+                         (uint64_t)a.K * 2, kBlockK, kMaxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != cudaSuccess) return e;
+    }
     p.A = a.A;
     p.W = a.W;
     p.S = a.S;
@@ -644,20 +690,23 @@ cudaError_t launch_decode(const GemmArgs& a) {
     p.K = a.K;
     p.group = a.group;
     p.err = device_error_word(dev);
-    p.counters = reinterpret_cast<unsigned*>(a.ws);
-    p.partials = reinterpret_cast<float4*>(a.ws + counters_bytes(a.N));
+    p.cs = cluster_size(reinterpret_cast<const void*>(ki.fn), ki.smem, a.N, a.K, a.wbits, dev);
     p.early_weights = (g_early_weights && !a.weights_just_written) ? 1 : 0;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid_ctas(a.N, a.K, a.wbits, dev));
+    cfg.gridDim = dim3((unsigned)(geo.NSG * p.cs));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = (size_t)ki.smem;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, ki.fn, p);
 }
 

@@ -28,12 +28,22 @@
 // dequantize-then-matmul.  A group holding Inf/NaN activations makes that
 // token's outputs NaN.
 //
-// Streaming is the same as the fp16 decode kernel (hq_decode.cu): one CTA per
-// SM over an equal share of the tile-order byte stream, a bulk-copy ring fed
-// by one producer warp (codes and scales before griddepcontrol.wait, the
-// activation pieces after it), eight consumer warps each owning one 16-column
-// strip, and strip groups shared between CTAs finished by the last CTA to
-// arrive (partials summed in CTA order; counters reset by that CTA).
+// Streaming.  The tile order stores the weights as units (strip group sg,
+// k-block kb) in sg-major order, each one contiguous span, so the tensor is one
+// byte stream; CTA c of G (two per SM) takes units [U c / G, U (c+1) / G), an
+// equal byte share whatever the shape.  A stage is up to 8 k-blocks of one
+// strip group: its 32 KB of codes arrive as ONE bulk copy (the TMA engine
+// charges a fixed cost per operation: 4 KB copies stream at a quarter of the
+// rate of 32 KB ones), while the small operands -- activation pieces, weight-
+// and activation-scale rows -- go as 16-byte cp.async spread over two producer
+// warps (a warp holding many DRAM-latency cp.async per lane stalls its issue).
+// Codes and weight scales are requested before griddepcontrol.wait,
+// activation pieces after it.  Eight consumer warps each own one 16-column
+// strip.  A strip group shared between CTAs is finished by the last CTA to
+// arrive: every sharer writes its fp32 partial, one thread fences and counts
+// the arrival, and the CTA that completes the count sums the partials in CTA
+// order after its main loop (deterministic) and resets the counter.  No CTA
+// waits on another; the workspace is zero-filled once, never per call.
 #include "hq_common.cuh"
 #include "hq_internal.h"
 #include "hq_layout.h"
@@ -42,19 +52,30 @@
 #include <type_traits>
 #include <utility>
 
+// Two CTAs per SM, each with a ~100 KB ring of two 32 KB-code stages, eight
+// consumer warps (one per strip) and two producer warps: measured fastest on
+// B200 among 1-2 CTAs per SM x 8-16 consumer warps x 1-4 producer warps.
 #ifndef HQ_DECODE_I8_CTAS_PER_SM
-#define HQ_DECODE_I8_CTAS_PER_SM 1
+#define HQ_DECODE_I8_CTAS_PER_SM 2
 #endif
 #ifndef HQ_DECODE_I8_RING_KB
-#define HQ_DECODE_I8_RING_KB 200
+#define HQ_DECODE_I8_RING_KB 100
+#endif
+#ifndef HQ_DECODE_I8_CONSUMERS
+#define HQ_DECODE_I8_CONSUMERS 8
+#endif
+#ifndef HQ_DECODE_I8_PRODUCERS
+#define HQ_DECODE_I8_PRODUCERS 2
 #endif
 
 namespace hq {
 
 namespace {
 
-constexpr int kNC = 16;  // consumer warps: warps w and w + 8 own strip w of a strip group
-constexpr int kProducerWarps = 2;  // warp kNC issues the code copy; both share the small operands
+constexpr int kNC = HQ_DECODE_I8_CONSUMERS;  // consumer warps: warps w, w + 8, ... own strip w of a strip group
+constexpr int kHalves = kNC / 8;             // warps per strip, each taking 1/kHalves of every stage
+constexpr int kProducerWarps = HQ_DECODE_I8_PRODUCERS;  // warp kNC issues the code copy; all share the small operands
+static_assert(kNC == 8 || kNC == 16, "one or two consumer warps per strip");
 constexpr int kProducerWarp = kNC;
 constexpr int kThreads = (kNC + kProducerWarps) * 32;
 constexpr int kUPS = 8;        // k-blocks per stage (32 KB of full-group codes: one bulk copy)
@@ -80,7 +101,7 @@ struct RingI8 {
     static constexpr int kXS = kS + kUPS * kSUnit;  // x scales: 16 token slots x fp32 per scale group
     static constexpr int kBytes = align_up(kXS + kUPS * 64, 128);
     static constexpr int kStages = clampi(kRingBudget / kBytes, 2, 8);
-    static constexpr int kPair = 2 * 8 * NT * 32 * 8;  // two buffers of half 1's sums (float2 per lane)
+    static constexpr int kPair = kHalves > 1 ? 2 * 8 * NT * 32 * 8 : 0;  // two buffers of half 1's sums (float2 per lane)
     static constexpr int kSmem = kStages * kBytes + kPair + 128 + 2 * kStages * 8 + 16;
 };
 
@@ -223,7 +244,7 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
 }
 
 template <int NT, typename ST, typename OT>
-__global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_constant__ I8Params p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const __grid_constant__ I8Params p) {
     using L = RingI8<NT, ST>;
     constexpr int kStages = L::kStages;
 
@@ -328,9 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ consumers
-    // Two warps per strip: half 0 takes the first kBatch k-blocks of every
-    // stage, half 1 the rest; their sums meet in shared memory when a strip
-    // group is done.
+    // kHalves warps per strip: with two, half 0 takes the first half of every
+    // stage's k-blocks and half 1 the rest, and their sums meet in shared
+    // memory when a strip group is done.
     pdl_wait();
     const int g = lane >> 2, t = lane & 3;
     const int sl = warp & 7, half = warp >> 3;
@@ -379,20 +400,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_con
     // which stores the group or, when other CTAs share it, writes the partial
     // and lets thread 0 count the arrival (the last arriver sums after the loop).
     auto flush_group = [&](int sg) {
-        float2* xch = pair_buf + ((nflush & 1) * 8 + sl) * (NT * 32);
-        ++nflush;
-        if (half == 1) {
+        if constexpr (kHalves > 1) {
+            float2* xch = pair_buf + ((nflush & 1) * 8 + sl) * (NT * 32);
+            ++nflush;
+            if (half == 1) {
 #pragma unroll
-            for (int j = 0; j < NT; ++j) xch[j * 32 + lane] = make_float2(facc[j][0], facc[j][1]);
-        }
-        named_bar_sync(kPairBar, kNC * 32);
-        if (half == 0) {
-#pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                const float2 v = xch[j * 32 + lane];
-                facc[j][0] += v.x;
-                facc[j][1] += v.y;
+                for (int j = 0; j < NT; ++j) xch[j * 32 + lane] = make_float2(facc[j][0], facc[j][1]);
             }
+            named_bar_sync(kPairBar, kNC * 32);
+            if (half == 0) {
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const float2 v = xch[j * 32 + lane];
+                    facc[j][0] += v.x;
+                    facc[j][1] += v.y;
+                }
+            }
+        }
+        if (half == 0) {
             const int width = geo.width(sg);
             const long long g0 = (long long)sg * KB, g1 = g0 + KB;
             if (g0 >= u_begin && g1 <= u_end) {
@@ -431,7 +456,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_con
         if (waits_ok) waits_ok = mbar_wait(&full[slot], (uint32_t)(it / kStages) & 1u, p.err);
         const uint8_t* stage = ring + slot * L::kBytes;
         const int width = geo.width(d.sg);
-        const int b0 = half * kBatch;  // this warp's k-blocks of the stage: [b0, min(b0 + kBatch, n))
+        constexpr int kPer = kUPS / kHalves;  // k-blocks of a stage per warp of the strip
+#pragma unroll
+        for (int bb = 0; bb < kPer; bb += kBatch) {
+        const int b0 = half * kPer + bb;  // this batch: k-blocks [b0, min(b0 + kBatch, n)) of the stage
         const int bn = d.n - b0 < kBatch ? d.n - b0 : kBatch;
         if (sl < width && bn > 0) {
             const uint32_t unit_bytes = (uint32_t)width * 512u;
@@ -463,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_i8_kernel(const __grid_con
                     flush_ints(stage, gl);
                 }
             }
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
@@ -541,6 +570,22 @@ std::pair<I8Fn, int> select_i8(const GemmArgs& a) {
 }
 
 size_t pieces_bytes(int K) { return (size_t)(K / kBlockK) * 4 * kTileBytes; }
+
+size_t counters_bytes(int N) {
+    const size_t nsg = (size_t)((N / kStripCols + kGroupStrips - 1) / kGroupStrips);
+    return (nsg * 4 + 255) & ~(size_t)255;
+}
+
+int grid_ctas(int N, int K, int dev) {
+    const long long U = TileGeom(K, N, 4).units();
+    const long long G = (long long)device_info(dev).sm_count * kCtasPerSm;
+    return (int)(U < G ? U : G);
+}
+
+// Counters, then two partial tiles per CTA (8 strips x 4 token tiles x 32 lanes x float2).
+size_t split_bytes(int N, int K, int dev) {
+    return counters_bytes(N) + (size_t)grid_ctas(N, K, dev) * 2 * 8 * 4 * 32 * sizeof(float2);
+}
 size_t xscale_bytes(int K) { return ((size_t)(K / kBlockK) * 64 + 255) & ~(size_t)255; }
 
 }  // namespace
@@ -552,14 +597,14 @@ bool decode_i8_supported(const GemmArgs& a) {
     return a.group % kBlockK == 0 && a.K % a.group == 0;
 }
 
-size_t decode_i8_extra_bytes(int K) { return pieces_bytes(K) + xscale_bytes(K); }
+size_t decode_i8_workspace_bytes(int N, int K, int dev) { return split_bytes(N, K, dev) + pieces_bytes(K) + xscale_bytes(K); }
 
 cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const size_t split = decode_split_bytes(a.N, a.K, 4, dev);
-    if (!a.ws || a.ws_bytes < split + decode_i8_extra_bytes(a.K)) return cudaErrorInvalidValue;
+    const size_t split = split_bytes(a.N, a.K, dev);
+    if (!a.ws || a.ws_bytes < decode_i8_workspace_bytes(a.N, a.K, dev)) return cudaErrorInvalidValue;
     const int NT = (a.M + kTokTile - 1) / kTokTile;
     int8_t* pieces = reinterpret_cast<int8_t*>(a.ws + split);
     float* xscale = reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K));
@@ -596,16 +641,14 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     p.C = a.C;
     p.err = device_error_word(dev);
     p.counters = reinterpret_cast<unsigned*>(a.ws);
-    p.partials = reinterpret_cast<float2*>(a.ws + decode_counters_bytes(a.N));
+    p.partials = reinterpret_cast<float2*>(a.ws + counters_bytes(a.N));
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
     p.group = a.group;
     p.early_weights = (early_weights && !a.weights_just_written) ? 1 : 0;
-    const long long U = TileGeom(a.K, a.N, 4).units();
-    const long long G = (long long)device_info(dev).sm_count * kCtasPerSm;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(U < G ? U : G));
+    cfg.gridDim = dim3((unsigned)grid_ctas(a.N, a.K, dev));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = (size_t)k.second;
     cfg.stream = a.stream;

@@ -39,16 +39,13 @@ cudaError_t ensure_smem_attr(const void* fn, int dev, int bytes);
 // 0 when such a cluster cannot be launched.
 int max_active_clusters(const void* fn, int threads, int smem, int cs, int dev);
 
-// Decode (M <= 16) HBM-streaming kernels.  Workspace: per-strip-group arrival
-// counters (decode_counters_bytes), then the split partials (together
-// decode_split_bytes), then, for the integer-MMA kernel, the activation pieces
-// and their scales (decode_i8_extra_bytes).
+// Decode (M <= 16) HBM-streaming kernels.  The workspace holds, for the
+// integer-MMA kernel only, per-strip-group arrival counters, the split
+// partials and the activation pieces with their scales.
 size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev);
-size_t decode_counters_bytes(int N);
-size_t decode_split_bytes(int N, int K, int wbits, int dev);
 // int4 codes x fp16/bf16 activations on the integer tensor cores (no bias).
 bool decode_i8_supported(const GemmArgs& a);
-size_t decode_i8_extra_bytes(int K);
+size_t decode_i8_workspace_bytes(int N, int K, int dev);
 cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights);
 bool decode_supported(const GemmArgs& a);
 // Programmatic dependent launch lets a decode GEMM stream its weights while the
