@@ -44,6 +44,13 @@ def weight_bytes(K, N, wbits=4, group=GROUP):
     return K * N * wbits // 8 + (K // group) * N * 2
 
 
+def kernels_per_gemm(M, K, N):
+    """Kernels one int4 decode hq_gemm launches (hq_decode.cu launch_decode): two for a wide layer
+    (>= 128 strip groups of 128 columns) at M <= 4 with 16-bit activations, which runs the
+    activation prep kernel before the integer-MMA kernel; one otherwise."""
+    return 2 if (M <= 4 and N // 128 >= 128) else 1
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -142,6 +149,132 @@ class CpuSweep:
                 return self.bytes_per_pass * passes / el / 1e12, el, passes
 
 
+class CpuTq1:
+    """The TQ1_0 GEMV (M = 1, fp32 x) on the host cores through the oracle's restatement of
+    kernel_gemv_tq1_0 (native_decoder.cu:155-206): the output projection (vocab 248320 x hidden
+    5120) and the four 27B layer shapes, the set the GPU's tq1_0 sub-object times.  Blocks are
+    seeded random trit bytes (< 243) with fp16 d in [0.01, 0.05)."""
+
+    SHAPES = [("output_proj", 5120, 248320)] + SHAPES
+
+    def __init__(self, nthreads: int):
+        import numpy as np
+        from oracle import oracle as o
+        self.o, self.nthreads = o, nthreads
+        rng = np.random.default_rng(5)
+        self.data = []
+        for name, K, N in self.SHAPES:
+            blob = rng.integers(0, 243, size=(N, K // 256, 56), dtype=np.uint8)
+            d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16)
+            blob[..., 0:2] = d.view(np.uint8).reshape(N, K // 256, 2)
+            blob[..., 54:56] = 0
+            x = rng.standard_normal(K).astype(np.float32)
+            self.data.append((K, N, blob.reshape(-1), x))
+        self.bytes_per_pass = sum(N * (K // 256) * 56 for _, K, N in self.SHAPES)
+
+    def one_pass(self):
+        for K, N, blob, x in self.data:
+            self.o.gemv_tq1_0(x, blob, K, N, nthreads=self.nthreads)
+
+    run = CpuSweep.run
+
+
+def reference_kernel_sweep(args):
+    """The reference's own CUDA kernels timed on this GPU beside hq_gemm on identical inputs.
+
+    kernel_marlin_gemm_int4_templated (marlin_gemm.cu:130-237, through
+    MarlinGemmEngine::forward_marlin_int4, :570-613, which also clears Y) and
+    kernel_baseline_int4_gemm (:76-117, through forward_baseline_int4, :552-568) from the
+    reference's unmodified marlin_gemm.cu compiled for sm_100a into
+    oracle/_ref/libref_marlin.so, at the four 27B layer shapes and M in {1, 2, 4, 8}, on the
+    reference's own conventions: fp32 X [M][K], fp32 scales and biases [K/128][N], fp32 Y; int4
+    codes as Marlin quads (marlin) or linear words (baseline).  hq_gemm gets the same codes in
+    tile order with the same fp32 X, scales and biases.  Each launch runs on the legacy default
+    stream, where the reference launches; CUDA events on that stream bracket `reps` launches
+    that rotate over enough weight copies that every copy was last read more than two L2 sizes
+    earlier.  GB/s counts the int4 codes plus fp32 scales and biases."""
+    import ctypes
+
+    import torch
+    from oracle import oracle as o
+    r = o.ref_lib()
+    if r is None:
+        return {"unavailable": "oracle/_ref/libref_marlin.so is not built (the reference sources were absent "
+                               "when the package was built)"}
+    from nebula_b200 import _lib, hq
+    vp = ctypes.c_void_p
+    r.ref_forward_marlin.argtypes = [vp] * 6 + [ctypes.c_uint32]
+    r.ref_forward_baseline.argtypes = [vp] * 6 + [ctypes.c_uint32]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ds = torch.cuda.default_stream(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    rows = []
+    L = _lib.lib()
+    for name, K, N in SHAPES:
+        nbytes = K * N // 2 + 2 * (K // GROUP) * N * 4
+        n_copies = min(32, -(-int(2.5 * L2_BYTES) // nbytes) + 1)
+        lin = [torch.randint(-2**31, 2**31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=g)
+               for _ in range(n_copies)]
+        # Marlin quad (marlin_gemm.cu:446-455): words 4q..4q+3 of column n side by side
+        quad = [w.view(K // 32, 4, N).permute(0, 2, 1).contiguous() for w in lin]
+        tile = [hq.repack(w.view(torch.uint8).reshape(-1), _lib.HQ_WFMT_LINEAR_U4, _lib.HQ_WFMT_TILE_U4, K, N)
+                for w in lin]
+        S = [(torch.rand((K // GROUP, N), device=dev, generator=g) * 0.01 + 0.005) for _ in range(n_copies)]
+        B = [-8.0 * s for s in S]
+        eng = r.ref_engine_create(8, K, N, GROUP)
+        if not eng:
+            return {"unavailable": "ref_engine_create failed: " + r.ref_last_error().decode()}
+        try:
+            for M in (1, 2, 4, 8):
+                X = torch.randn((M, K), device=dev, generator=g)
+                Y = torch.empty((M, N), device=dev)
+                ws = hq.make_workspace(M, N, K, GROUP, _lib.HQ_WFMT_TILE_U4, dev)
+
+                def marlin(c):
+                    if r.ref_forward_marlin(vp(eng), vp(X.data_ptr()), vp(quad[c].data_ptr()), vp(S[c].data_ptr()),
+                                            vp(B[c].data_ptr()), vp(Y.data_ptr()), M) != 0:
+                        raise RuntimeError(r.ref_last_error().decode())
+
+                def baseline(c):
+                    if r.ref_forward_baseline(vp(eng), vp(X.data_ptr()), vp(lin[c].data_ptr()), vp(S[c].data_ptr()),
+                                              vp(B[c].data_ptr()), vp(Y.data_ptr()), M) != 0:
+                        raise RuntimeError(r.ref_last_error().decode())
+
+                def ours(c):
+                    st = L.hq_gemm(vp(X.data_ptr()), _lib.HQ_F32, vp(tile[c].data_ptr()), _lib.HQ_WFMT_TILE_U4,
+                                   vp(S[c].data_ptr()), _lib.HQ_F32, vp(B[c].data_ptr()), vp(Y.data_ptr()),
+                                   _lib.HQ_F32, M, N, K, GROUP, vp(ws.data_ptr()), ws.numel(), None)
+                    if st != 0:
+                        raise RuntimeError(L.hq_last_error_string().decode())
+                row = {"shape": name, "M": M, "K": K, "N": N, "copies": n_copies}
+                reps = max(10, n_copies)
+                for key, fn in (("ref_marlin", marlin), ("ref_baseline", baseline), ("hq", ours)):
+                    ms = _time_launches(torch, ds, fn, n_copies, reps=reps)
+                    row[key + "_us"] = round(ms * 1e3, 2)
+                    row[key + "_GBps"] = round(nbytes / (ms / 1e3) / 1e9, 1)
+                row["hq_over_ref_marlin"] = round(row["ref_marlin_us"] / row["hq_us"], 2)
+                row["hq_over_ref_baseline"] = round(row["ref_baseline_us"] / row["hq_us"], 2)
+                rows.append(row)
+                del X, Y, ws
+        finally:
+            torch.cuda.synchronize()
+            r.ref_engine_destroy(vp(eng))
+        del lin, quad, tile, S, B
+        torch.cuda.empty_cache()
+    hq.check_device_error()
+    tot = {k: sum(rw[k + "_us"] for rw in rows) for k in ("ref_marlin", "ref_baseline", "hq")}
+    return {"rows": rows, "sum_us": {k: round(v, 1) for k, v in tot.items()},
+            "hq_over_ref_marlin": round(tot["ref_marlin"] / tot["hq"], 2),
+            "hq_over_ref_baseline": round(tot["ref_baseline"] / tot["hq"], 2),
+            "timing": "per row: CUDA events on the legacy default stream around max(10, copies) launches queued "
+                      "behind a spin kernel (device time, back to back) after 3 warm-up launches; the reference's "
+                      "Y memset included",
+            "note": "the reference's CUDA kernels on this GPU: a comparison beside this arm's CPU value, not "
+                    "part of it"}
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -164,6 +297,13 @@ def run_reference_arm(args):
                              "sample": "one full pass of the decode sweep (20 GEMMs) per step: the oracle's "
                                        "dequant-then-matmul (fp32, OpenMP) on all host threads"},
             "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_ref_kernels:
+        try:
+            import torch
+            gpu = torch.cuda.is_available()
+        except ImportError:
+            gpu = False
+        line["reference_kernels"] = reference_kernel_sweep(args) if gpu else {"unavailable": "no GPU visible"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -171,17 +311,22 @@ def run_reference_arm(args):
 # ------------------------------------------- prefill / ternary sub-sweeps
 
 def _time_launches(torch, stream, fn, n_copies, reps=10, warmup=3):
-    """Average device time (ms) of fn(copy) over `reps` launches, CUDA events on `stream`."""
+    """Average device time (ms) of fn(copy) over `reps` launches, CUDA events on `stream`.
+
+    A ~5 ms spin kernel is queued ahead of the timed launches, so that the host has queued all of
+    them before the first one starts: the events then bracket the launches running back to back
+    on the device, not the host's per-call overhead."""
     with torch.cuda.stream(stream):
         for w in range(warmup):
             fn(w % n_copies)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     with torch.cuda.stream(stream):
+        torch.cuda._sleep(10_000_000)
+        e0.record(stream)
         for r in range(reps):
             fn(r % n_copies)
-    e1.record(stream)
+        e1.record(stream)
     e1.synchronize()
     return e0.elapsed_time(e1) / reps
 
@@ -266,11 +411,12 @@ def tq1_sweep(torch, L, _lib, dev, stream, peaks, args):
                 fn(n_copies - 1 - c)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
         with torch.cuda.stream(stream):
+            torch.cuda._sleep(10_000_000)  # the host queues every timed launch before the first runs
+            e0.record(stream)
             for r in range(reps):
                 fn(r % n_copies)
-        e1.record(stream)
+            e1.record(stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / reps
         rows.append({"shape": name, "K": K, "N": N, "copies": n_copies, "us": round(ms * 1e3, 2),
@@ -281,8 +427,8 @@ def tq1_sweep(torch, L, _lib, dev, stream, peaks, args):
     gbps = tot_b / (tot_ms / 1e3) / 1e9
     return {"metric": "TQ1_0 GEMV GB/s (M=1, fp32 x)", "value": gbps, "unit": "GB/s",
             "frac_hbm": gbps / peaks["hbm_gbs"], "per_gemv": rows,
-            "timing": "per shape: CUDA events around max(10, copies) launches after 3 warm-up launches on "
-                      "other copies; launch gaps included"}
+            "timing": "per shape: CUDA events around max(10, copies) launches queued behind a spin kernel "
+                      "(device time, back to back) after 3 warm-up launches on other copies"}
 
 
 def proj_sweep(torch, L, _lib, dev, stream, peaks, args):
@@ -396,8 +542,8 @@ def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
     return {"metric": "ternary W2A16 GEMM (BASELINE configs[3])",
             "decode_GBps": dec, "decode_frac_hbm": dec / peaks["hbm_gbs"],
             "prefill_TFLOPS": pf, "prefill_frac_tensor": pf / peaks["bf16_tflops"], "dtype": "f16",
-            "timing": "per GEMM: CUDA events around 20 (M<=16) / 10 launches after 3 warm-up, 2 rotating weight "
-                      "copies (not graph-captured, launch gaps included)",
+            "timing": "per GEMM: CUDA events around 20 (M<=16) / 10 launches queued behind a spin kernel, after 3 "
+                      "warm-up, 2 rotating weight copies (not graph-captured)",
             "per_gemm": rows}
 
 
@@ -583,9 +729,13 @@ def main():
     ap.add_argument("--impl", default="hq", choices=["hq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--copies", type=int, default=2, help="rotating weight copies per shape (defeats L2)")
+    ap.add_argument("--copies", type=int, default=len(MS),
+                    help="weight copies per shape; the GEMM of a step at the i-th M reads copy i mod copies, so with "
+                         "the default (one per M) every GEMM of a step reads its own weights")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill and ternary sweeps")
     ap.add_argument("--no-stack", action="store_true", help="skip the TP layer stack (configs[4])")
+    ap.add_argument("--no-ref-kernels", action="store_true",
+                    help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--case", default=None,
                     help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits; "
                          "'tq1,K,N' runs hq_tq1_0_gemv, 'proj,TYPE,K,N' hq_output_projection instead")
@@ -664,11 +814,14 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     sh = stream.cuda_stream
 
-    def step(copy, timing_events=None):
+    def copy_of(M):
+        return MS.index(M) % args.copies
+
+    def step(timing_events=None):
         for i, (name, M, Kl, Nl, ar) in enumerate(gemms):
             if timing_events is not None:
                 timing_events[i][0].record(stream)
-            C = launch(name, M, copy, sh)
+            C = launch(name, M, copy_of(M), sh)
             if timing_events is not None:
                 timing_events[i][1].record(stream)
             if ar:
@@ -677,18 +830,16 @@ def main():
     # warm-up (also sets kernel attributes before graph capture)
     with torch.cuda.stream(stream):
         for w in range(args.warmup):
-            step(w % args.copies)
+            step()
     torch.cuda.synchronize()
 
-    # Capture one graph per weight copy: a step replays one graph.
+    # One graph holds a whole step.
     graphs = []
-    for c in range(args.copies):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            step(c)
-        graphs.append(gr)
-    for c in range(args.copies):
-        graphs[c].replay()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        step()
+    graphs.append(gr)
+    graphs[0].replay()
     torch.cuda.synchronize()
 
     # ---------------------------------------------------------- timed region
@@ -701,7 +852,7 @@ def main():
         ev0.record(stream)
         for s in range(args.steps):
             with torch.cuda.stream(stream):
-                graphs[s % args.copies].replay()
+                graphs[0].replay()
         ev1.record(stream)
         ev1.synchronize()
     torch.cuda.synchronize()
@@ -718,16 +869,18 @@ def main():
 
     # ----------------------------------------------- per-launch kernel timing
     # Every GEMM of a step bracketed by events on its stream (no graph, no
-    # collectives): the decode kernel's average launch duration per shape.
+    # collectives), all queued behind a spin kernel so that they run back to
+    # back on the device: the decode kernels' average launch duration per shape.
     per = []
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in gemms]
     reps = max(3, min(args.steps, 10))
     acc_ms = [0.0] * len(gemms)
     with torch.cuda.stream(stream):
         for r in range(reps):
+            torch.cuda._sleep(10_000_000)
             for i, (name, M, Kl, Nl, ar) in enumerate(gemms):
                 evs[i][0].record(stream)
-                launch(name, M, r % args.copies, sh)
+                launch(name, M, copy_of(M), sh)
                 evs[i][1].record(stream)
             torch.cuda.synchronize()
             for i in range(len(gemms)):
@@ -760,23 +913,22 @@ def main():
     h2d = sum(hostA[M][n].numel() * 2 for (n, M, _, _, _) in gemms)
     d2h = sum(hostC[M][n].numel() * 2 for (n, M, _, _, _) in gemms)
 
-    def e2e_step(copy):
+    def e2e_step():
         for (name, M, Kl, Nl, ar) in gemms:
             acts[M][name].copy_(hostA[M][name], non_blocking=True)
-            C = launch(name, M, copy, sh)
+            C = launch(name, M, copy_of(M), sh)
             if ar:
                 dist.all_reduce(C)
             hostC[M][name].copy_(C, non_blocking=True)
 
     with torch.cuda.stream(stream):
         for w in range(3):
-            e2e_step(w % args.copies)
+            e2e_step()
     e2e_graphs = []
-    for c in range(args.copies):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            e2e_step(c)
-        e2e_graphs.append(gr)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        e2e_step()
+    e2e_graphs.append(gr)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -784,7 +936,7 @@ def main():
     e0.record(stream)
     for s in range(args.steps):
         with torch.cuda.stream(stream):
-            e2e_graphs[s % args.copies].replay()
+            e2e_graphs[0].replay()
     e1.record(stream)
     e1.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -814,9 +966,17 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nth = os.cpu_count() or 1
         v, el, passes = CpuSweep(nth).run(args.cpu_seconds)
+        v1, el1, passes1 = CpuSweep(1).run(args.cpu_seconds / 4)
+        tq, elt, passest = CpuTq1(nth).run(args.cpu_seconds / 4)
         cpu = {"value": v, "unit": "TB/s", "cores": nth, "kind": "port",
                "sample": f"{passes} full pass(es) of the decode sweep (20 GEMMs) in {el:.1f} s: oracle "
-                         "dequant-then-matmul, fp32 OpenMP, all host threads"}
+                         "dequant-then-matmul, fp32 OpenMP, all host threads",
+               "one_thread": {"value": v1, "unit": "TB/s", "cores": 1,
+                              "sample": f"{passes1} full pass(es) of the same sweep in {el1:.1f} s on one thread"},
+               "tq1_0": {"value": tq * 1e3, "unit": "GB/s", "cores": nth, "kind": "port",
+                         "sample": f"{passest} pass(es) of the TQ1_0 GEMV set of the tq1_0 sub-object (output "
+                                   f"projection + four layer shapes, M = 1, fp32 x) in {elt:.1f} s: the oracle's "
+                                   "restatement of kernel_gemv_tq1_0, all host threads"}}
 
     for gr in graphs + e2e_graphs:
         del gr
@@ -832,17 +992,21 @@ def main():
             "config": {"workload": "decode_sweep (BASELINE configs[1]): 27B layer QKV 5120x7168, O 5120x5120, "
                                    "gate_up 5120x34816, down 17408x5120 at M in {1,2,4,8,16}; int4 g128, fp16 A",
                        "global_batch": "M in {1,2,4,8,16}", "parallelism": f"tp{world}" if world > 1 else "single",
-                       "l2": f"inputs larger than L2: {args.copies} rotating weight copies per shape "
-                             f"({args.copies * layer_bytes / 1e6:.0f} MB)",
+                       "l2": f"inputs larger than L2: {args.copies} weight copies per shape "
+                             f"({args.copies * layer_bytes / 1e6:.0f} MB); the GEMM at the i-th M reads copy i, so "
+                             "every GEMM of a step reads weights no other GEMM of the step touched",
                        "graph": "each step is one CUDA graph replay"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": peaks["source"], "frac_of_nominal_8000": achieved / 8000.0,
-                         "kernel": "hq decode kernels (mma.sync for M <= 8 / narrow layers, tcgen05 for M > 8 on wide layers)", "traffic_unit": "bytes per launch (avg)",
+                         "kernel": "hq decode kernels: integer-MMA stream kernel (wide layers at M <= 4), "
+                                   "cluster split-K mma.sync kernel (narrow layers, M <= 8), tcgen05 kernel "
+                                   "(M > 8 on wide layers)",
+                         "traffic_unit": "bytes per launch (avg)",
                          "algorithmic_bytes_per_step": kern_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": len(gemms) * args.steps,
+            "gpu_launches": sum(kernels_per_gemm(M, Kl, Nl) for (_, M, Kl, Nl, _) in gemms) * args.steps,
             "clocks": clocks.summary(),
             "per_gemm": per,
         }

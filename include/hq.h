@@ -105,10 +105,18 @@ HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t
  *                   w = u * scale[g][n] + bias[g][n]     (bias != NULL; reference
  *                                                          form, marlin_gemm.cu:208-209)
  *            ternary w = t * scale[g][n]
- *   a_dtype: HQ_F16 | HQ_BF16 | HQ_F32 (f32 activations are split into two fp16
- *            terms on chip, so the product keeps ~fp32 accuracy)
- *   s_dtype: HQ_F16 | HQ_BF16 | HQ_F32; bias is always f32
- *   c_dtype: HQ_F16 | HQ_BF16 | HQ_F32
+ *   a_dtype: HQ_F16 | HQ_BF16 | HQ_F32.  f32 activations keep ~fp32 accuracy:
+ *            held on chip as two fp16 terms or, at M <= 4, as two fixed-point
+ *            parts of 15 bits per (token, scale group), 30 bits in all.  At
+ *            M <= 4 on layers of >= 16384 columns, 16-bit activations are held
+ *            as one 15-bit fixed-point copy per (token, scale group): the
+ *            result stays within ~1e-5 of max|C| of the fp32 product.  A scale
+ *            group of activations holding Inf/NaN makes that token's outputs NaN.
+ *   s_dtype: HQ_F16 | HQ_BF16 | HQ_F32; bias is always f32.  Combinations
+ *            (activations, scales): (f16, f16), (bf16, bf16), (f16 | bf16 | f32,
+ *            f32), (f32, f16); a bias goes with f32 scales and f16 / f32
+ *            activations.  Ternary weights: (f16, f16), (bf16, bf16).
+ *   c_dtype: HQ_F16 | HQ_BF16 | HQ_F32: the activation type, or f32
  *   wfmt:    HQ_WFMT_TILE_U4 / HQ_WFMT_TILE_T2 run directly.  LINEAR_U4,
  *            MARLIN_QUAD and LINEAR_T2 are accepted for drop-in use and are
  *            re-tiled into the workspace first (one extra pass over the

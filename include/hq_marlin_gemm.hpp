@@ -6,15 +6,20 @@
 // device-pointer arguments, fp32 X / scales / biases / Y, w = u*scale + bias,
 // Y overwritten, asynchronous on the legacy default stream, std::runtime_error
 // on a CUDA failure.  Differences (documented, deliberate):
-//   * weights handed to forward_marlin_int4 / forward_baseline_int4 in the
-//     reference layouts are re-tiled on device into an engine-owned buffer
-//     on every call; hq_repack_* + hq_gemm on tile-order weights skip that pass;
+//   * Marlin-quad weights handed to forward_marlin_int4 are re-tiled on
+//     device into an engine-owned buffer on every call; hq_repack_* + hq_gemm
+//     on tile-order weights skip that pass;
 //   * M up to any value (the reference silently overflows for M > 8,
 //     marlin_gemm.cu:260,304);
 //   * bandwidth_utilization_pct is relative to kPeakBandwidthGBs (B200
 //     nominal HBM3e) instead of the RTX 4070's 504 GB/s (:677);
 //   * forward_cutlass_int8 sums the dp4a products exactly in int32 and rounds
 //     once (the reference rounds an fp32 running sum per 4 k), any M.
+// forward_baseline_int4 keeps the reference's role: an un-optimised scalar
+// kernel on the linear layout, the comparator of run_benchmark_sweep's
+// speedup_ratio (use forward_marlin_int4 or hq_gemm for speed).
+// The class is exported from libhq.so, so a program written against the
+// reference header links against it unchanged.
 #pragma once
 
 #include <cstddef>
@@ -54,7 +59,7 @@ struct MarlinRepackResult {
     bool repack_under_1s = true;
 };
 
-class MarlinGemmEngine {
+class __attribute__((visibility("default"))) MarlinGemmEngine {
 public:
     static constexpr double kPeakBandwidthGBs = 7700.0;
 

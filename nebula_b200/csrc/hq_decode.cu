@@ -638,6 +638,15 @@ int cluster_size(const void* fn, int smem, int N, int K, int wbits, int dev) {
 
 bool g_early_weights = true;
 
+// Smallest layer the integer-MMA stream kernel takes: in strip groups of 128
+// columns for 16-bit activations, in (strip group, k-block) units for fp32.
+#ifndef HQ_DECODE_I8_MIN_NSG
+#define HQ_DECODE_I8_MIN_NSG 128
+#endif
+#ifndef HQ_DECODE_I8_MIN_UNITS_F32
+#define HQ_DECODE_I8_MIN_UNITS_F32 8192
+#endif
+
 }  // namespace
 
 void set_decode_launch_overlap(bool on) { g_early_weights = on; }
@@ -660,8 +669,14 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // 34816: 26.2 us against 28.0 here): its consumer spends ~3x fewer
     // instructions per byte of codes.  Narrow layers, and M > 4, keep this
     // kernel, whose cluster split-K has a shorter start-up and tail.
-    if (a.M <= 4 && TileGeom(a.K, a.N, a.wbits).NSG >= 128 && decode_i8_supported(a))
-        return launch_decode_i8(a, g_early_weights);
+    // fp32 activations take it for large layers (>= 8192 k-block units, 32 MB of
+    // codes: 27B down 17408 x 5120 at 27.9 us against 42.0 here, gate_up 36.1
+    // against 56.3): this kernel splits them into two fp16 halves and runs
+    // twice the MMAs.  Smaller fp32 layers stay here (QKV 17.8 us against 19.4).
+    const TileGeom tg(a.K, a.N, a.wbits);
+    const bool i8_shape = a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
+                                                  : tg.NSG >= HQ_DECODE_I8_MIN_NSG;
+    if (a.M <= 4 && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
     // M > 8 on wide layers runs on tcgen05: the mma.sync kernel needs two token
     // tiles there and the tensor-memory kernel's cost does not depend on M.
     // Narrow layers (few strip groups) and M <= 8 stream faster here.

@@ -68,6 +68,7 @@
 #define HQ_DECODE_I8_PRODUCERS 2
 #endif
 
+
 namespace hq {
 
 namespace {
@@ -91,15 +92,21 @@ constexpr int kPrepThreads = 256;  // 16 token slots x 16 threads
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 constexpr int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); }
 
+// Stage layout.  With fp32 scales the stage also carries, per scale group, the
+// activation sums of the 16 token slots and the group's fp32 bias row (the
+// reference's u * s + b form; read only when the call has a bias).
 template <int NT, typename ST>
 struct RingI8 {
+    static constexpr bool kBias = std::is_same<ST, float>::value;
     static constexpr int kW = kUPS * kGroupStrips * 512;  // codes
     static constexpr int kXUnit = NT * kTileBytes;       // pieces of one k-block
     static constexpr int kX = kW;
     static constexpr int kSUnit = kGroupCols * (int)sizeof(ST);  // one scale row of the group's columns
     static constexpr int kS = kX + kUPS * kXUnit;
     static constexpr int kXS = kS + kUPS * kSUnit;  // x scales: 16 token slots x fp32 per scale group
-    static constexpr int kBytes = align_up(kXS + kUPS * 64, 128);
+    static constexpr int kXQ = kXS + kUPS * 64;     // x sums: 16 token slots x fp32 per scale group
+    static constexpr int kB = kXQ + (kBias ? kUPS * 64 : 0);  // bias rows (fp32), as the scale rows
+    static constexpr int kBytes = align_up(kB + (kBias ? kUPS * kSUnit : 0), 128);
     static constexpr int kStages = clampi(kRingBudget / kBytes, 2, 8);
     static constexpr int kPair = kHalves > 1 ? 2 * 8 * NT * 32 * 8 : 0;  // two buffers of half 1's sums (float2 per lane)
     static constexpr int kSmem = kStages * kBytes + kPair + 128 + 2 * kStages * 8 + 16;
@@ -108,8 +115,10 @@ struct RingI8 {
 struct alignas(16) I8Params {
     const uint8_t* W;
     const void* S;
+    const float* bias;     // [K/group][N] fp32, or null
     const int8_t* pieces;  // [K/64][NT*4 tokens][2][4][16] (workspace)
     const float* xscale;   // [K/group][16] 2^-s per (group, token slot) (workspace)
+    const float* xsum;     // [K/group][16] sum of x per (group, token slot) (workspace; read with a bias)
     void* C;
     unsigned* err;
     unsigned* counters;  // [NSG]
@@ -164,58 +173,90 @@ __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ uint32_t q16_hi(uint32_t w) { return lop3<(0xF0 & 0xCC) ^ 0xAA>(w, 0xF0F0F0F0u, 0x80808080u); }
 __device__ __forceinline__ uint32_t q16_lo(uint32_t w) { return lop3<(0xF0 & 0xCC) ^ 0xAA>(w << 4, 0xF0F0F0F0u, 0x80808080u); }
 
+// Eight consecutive activations as fp32 (16-byte aligned).
+template <typename AT>
+__device__ __forceinline__ void load8(const AT* p, float (&f)[8]) {
+    if constexpr (sizeof(AT) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        const AT* e = reinterpret_cast<const AT*>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = to_f32(e[i]);
+    }
+}
+
 // Activation pieces.  One CTA per scale group, 16 threads per token slot, 8
 // consecutive k per thread.  Writes the pieces of token slots [0, slots) (zero
-// beyond M) and 2^-s of all 16 slots of the group.
-template <typename AT>
+// beyond M), 2^-s of all 16 slots of the group and, with `sums`, the group's
+// sum of x per slot.
+//
+// RES (fp32 activations): x keeps 30 bits as two fixed-point copies.  Slot m <
+// slots/2 holds token m as above, x_hi = 2^-s round(2^s x); slot slots/2 + m
+// holds the rest, x - x_hi (exact in fp32, |x - x_hi| <= 2^-s-1), in steps of
+// 2^-(s+15).  Both slots of a token land in the same lanes (tiles j and
+// j + NT/2), whose sums the GEMM adds before storing.
+template <typename AT, bool RES>
 __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restrict__ A, int M, int K, int group,
                                                               int slots, int8_t* __restrict__ pieces,
-                                                              float* __restrict__ xscale) {
+                                                              float* __restrict__ xscale, float* __restrict__ xsum) {
     if (threadIdx.x == 0) pdl_launch_dependents();
     // A may come from the previous kernel, and that kernel may still read the
     // pieces of the previous call.
     pdl_wait();
     const int gi = blockIdx.x;
     const int m = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+    const bool res = RES && m >= slots / 2 && m < slots;
+    const int tok = res ? m - slots / 2 : m;  // the token whose values this slot holds
     const int oct = group / 8;
-    const AT* row = A + (size_t)m * K + (size_t)gi * group;
-    float mx = 0.f;
+    const AT* row = A + (size_t)tok * K + (size_t)gi * group;
+    float mx = 0.f, sum = 0.f;
     int bad = 0;
-    if (m < M) {
+    if (tok < M) {
         for (int o = l16; o < oct; o += 16) {
-            const uint4 v = *reinterpret_cast<const uint4*>(row + 8 * o);
-            const AT* e = reinterpret_cast<const AT*>(&v);
+            float f[8];
+            load8(row + 8 * o, f);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float f = to_f32(e[i]);
-                bad |= !isfinite(f);
-                mx = fmaxf(mx, fabsf(f));
+                bad |= !isfinite(f[i]);
+                mx = fmaxf(mx, fabsf(f[i]));
+                sum += f[i];
             }
         }
     }
 #pragma unroll
     for (int d = 8; d >= 1; d >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+        sum += __shfl_xor_sync(0xffffffffu, sum, d);
         bad |= __shfl_xor_sync(0xffffffffu, bad, d);
     }
-    // x * 2^s < 2^14 for every |x| <= mx, so |x_fixed| <= 2^14 and h = (x_fixed + 128) >> 8 <= 64.
+    // x * 2^s < 2^14 for every |x| <= mx, so |x_fixed| <= 2^14 and h = (x_fixed + 128) >> 8 <= 64;
+    // the rest of a RES slot is below 2^-s-1, so (x - x_hi) * 2^(s+15) <= 2^14 as well.
     int s = 0;
     float xs = 0.f;
     if (bad) {
-        xs = __int_as_float(0x7fc00000);
+        xs = res ? 0.f : __int_as_float(0x7fc00000);
     } else if (mx > 0.f) {
         s = 13 - ilogbf(mx);
-        xs = ldexpf(1.f, -s);
+        xs = ldexpf(1.f, res ? -(s + 15) : -s);
     }
-    if (l16 == 0) xscale[(size_t)gi * 16 + m] = m < M ? xs : 0.f;
+    if (l16 == 0) {
+        xscale[(size_t)gi * 16 + m] = tok < M ? xs : 0.f;
+        if (xsum) xsum[(size_t)gi * 16 + m] = (tok < M && !res) ? sum : 0.f;
+    }
     if (m >= slots) return;
     for (int o = l16; o < oct; o += 16) {
         int xf[8];
-        if (m < M && !bad) {
-            const uint4 v = *reinterpret_cast<const uint4*>(row + 8 * o);
-            const AT* e = reinterpret_cast<const AT*>(&v);
+        if (tok < M && !bad) {
+            float f[8];
+            load8(row + 8 * o, f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xf[i] = (int)rintf(ldexpf(to_f32(e[i]), s));
+            for (int i = 0; i < 8; ++i) {
+                const float hi = rintf(ldexpf(f[i], s));
+                xf[i] = res ? (int)rintf(ldexpf(f[i] - ldexpf(hi, -s), s + 15)) : (int)hi;
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) xf[i] = 0;
@@ -243,7 +284,9 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
     }
 }
 
-template <int NT, typename ST, typename OT>
+// RES: fp32 activations in two slots per token (x_prep_kernel); tiles j and
+// j + NT/2 hold the two parts of the same tokens.
+template <int NT, bool RES, typename ST, typename OT>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const __grid_constant__ I8Params p) {
     using L = RingI8<NT, ST>;
     constexpr int kStages = L::kStages;
@@ -277,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
     if (warp >= kProducerWarp) {
         // --------------------------------------------------------- producers
         // A warp holding more than a few DRAM-latency cp.async per lane stalls
-        // its issue; four warps share them so that none does.
-        const int pl = (warp - kProducerWarp) * 32 + lane;  // producer lane 0..127
+        // its issue; the producer warps share them so that none does.
+        const int pl = (warp - kProducerWarp) * 32 + lane;  // producer lane 0 .. 32 * kProducerWarps - 1
         const uint64_t pol = l2_policy_evict_first();
         const uint8_t* Sb = reinterpret_cast<const uint8_t*>(p.S);
         auto stage_ptr = [&](int it) { return ring + (it % kStages) * L::kBytes; };
@@ -299,6 +342,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
                 const int r = i / s_chunks, cidx = i - r * s_chunks;
                 const size_t off = (size_t)(g_first + r) * p.N + (size_t)d.sg * kGroupCols;
                 cp_async16(st + L::kS + r * L::kSUnit + 16 * cidx, Sb + off * sizeof(ST) + 16 * cidx);
+                if constexpr (L::kBias)
+                    if (p.bias)
+                        cp_async16(st + L::kB + r * L::kSUnit + 16 * cidx,
+                                   reinterpret_cast<const uint8_t*>(p.bias) + off * 4 + 16 * cidx);
             }
         };
         // Activation pieces and their scales (written by the preceding kernel), then
@@ -310,8 +357,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             const int p_chunks = d.n * NT * kTileBytes / 16;
             const int8_t* psrc = p.pieces + (size_t)d.kb * NT * kTileBytes;
             for (int i = pl; i < p_chunks; i += 32 * kProducerWarps) cp_async16(st + L::kX + 16 * i, psrc + 16 * i);
-            for (int i = pl; i < ng * 4; i += 32 * kProducerWarps)
+            for (int i = pl; i < ng * 4; i += 32 * kProducerWarps) {
                 cp_async16(st + L::kXS + 16 * i, p.xscale + (size_t)g_first * 16 + 4 * i);
+                if constexpr (L::kBias)
+                    if (p.bias) cp_async16(st + L::kXQ + 16 * i, p.xsum + (size_t)g_first * 16 + 4 * i);
+            }
             cp_async_mbar_arrive(&full[slot]);
         };
         Walker wk(u_begin, u_end, KB, kUPS);
@@ -384,6 +434,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
         }
     };
 
+    // Bias term of scale group gl of the stage, added once per group (at its first
+    // k-block): w = u s + b = q s + (8 s + b) with q = u - 8, so
+    // sum_k x_k w_k = s sum_k x_k q_k + (8 s + b) sum_k x_k.
+    auto add_bias = [&](const uint8_t* stage, int gl) {
+        if constexpr (L::kBias) {
+            const int nl = sl * kStripCols + g;
+            const float* sp = reinterpret_cast<const float*>(stage + L::kS + gl * L::kSUnit);
+            const float* bp = reinterpret_cast<const float*>(stage + L::kB + gl * L::kSUnit);
+            const float c0 = fmaf(8.f, sp[nl], bp[nl]), c1 = fmaf(8.f, sp[nl + 8], bp[nl + 8]);
+            const float* xq = reinterpret_cast<const float*>(stage + L::kXQ + gl * 64);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const float xsj = xq[kTokTile * j + t];
+                facc[j][0] = fmaf(xsj, c0, facc[j][0]);
+                facc[j][1] = fmaf(xsj, c1, facc[j][1]);
+            }
+        }
+    };
+
     auto store_pair = [&](int sg, int j, float v0, float v1) {
         const int n = sg * kGroupCols + sl * kStripCols + g;
         const int tok = kTokTile * j + t;
@@ -400,6 +469,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
     // which stores the group or, when other CTAs share it, writes the partial
     // and lets thread 0 count the arrival (the last arriver sums after the loop).
     auto flush_group = [&](int sg) {
+        if constexpr (RES) {
+#pragma unroll
+            for (int j = 0; j < NT / 2; ++j) {
+                facc[j][0] += facc[j + NT / 2][0];
+                facc[j][1] += facc[j + NT / 2][1];
+            }
+        }
         if constexpr (kHalves > 1) {
             float2* xch = pair_buf + ((nflush & 1) * 8 + sl) * (NT * 32);
             ++nflush;
@@ -475,6 +551,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
 #pragma unroll
             for (int u = 0; u < kBatch; ++u) {
                 if (u >= bn) break;
+                if constexpr (L::kBias)
+                    if (p.bias && (d.kb + b0 + u) % upg == 0) add_bias(stage, gl);
                 const uint32_t l0 = q16_lo(wv[u].x), l1 = q16_lo(wv[u].z), l2 = q16_lo(wv[u].y), l3 = q16_lo(wv[u].w);
                 const uint32_t h0 = q16_hi(wv[u].x), h1 = q16_hi(wv[u].z), h2 = q16_hi(wv[u].y), h3 = q16_hi(wv[u].w);
 #pragma unroll
@@ -513,15 +591,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             float2 sum[NT];
 #pragma unroll
             for (int j = 0; j < NT; ++j) sum[j] = make_float2(0.f, 0.f);
-            for (int q = c_first; q <= c_last; ++q) {
-                const int qslot = (int)(range_begin(U, G, q) / KB) == sg ? 0 : 1;
-                const float2* src = p.partials + (((size_t)q * 2 + qslot) * 8 + sl) * (NT * 32);
+            // Up to kFix partials in flight at once (one L2 round trip per batch), summed
+            // in CTA order.
+            constexpr int kFix = NT <= 2 ? 8 : 4;
+            for (int q0 = c_first; q0 <= c_last; q0 += kFix) {
+                float2 v[kFix][NT];
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
-                    const float2 v = __ldcg(src + j * 32 + lane);
-                    sum[j].x += v.x;
-                    sum[j].y += v.y;
+                for (int i = 0; i < kFix; ++i) {
+                    const int q = q0 + i;
+                    if (q <= c_last) {
+                        const int qslot = (int)(range_begin(U, G, q) / KB) == sg ? 0 : 1;
+                        const float2* src = p.partials + (((size_t)q * 2 + qslot) * 8 + sl) * (NT * 32);
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) v[i][j] = __ldcg(src + j * 32 + lane);
+                    }
                 }
+#pragma unroll
+                for (int i = 0; i < kFix; ++i)
+                    if (q0 + i <= c_last)
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) {
+                            sum[j].x += v[i][j].x;
+                            sum[j].y += v[i][j].y;
+                        }
             }
             if (sl < geo.width(sg))
 #pragma unroll
@@ -540,18 +632,18 @@ namespace {
 
 using I8Fn = void (*)(I8Params);
 
-template <int NT, typename ST, typename OT>
+template <int NT, bool RES, typename ST, typename OT>
 std::pair<I8Fn, int> i8_kernel() {
-    return {decode_i8_kernel<NT, ST, OT>, RingI8<NT, ST>::kSmem};
+    return {decode_i8_kernel<NT, RES, ST, OT>, RingI8<NT, ST>::kSmem};
 }
 
 template <typename ST, typename OT>
 std::pair<I8Fn, int> pick_nt(int NT) {
     switch (NT) {
-        case 1: return i8_kernel<1, ST, OT>();
-        case 2: return i8_kernel<2, ST, OT>();
-        case 3: return i8_kernel<3, ST, OT>();
-        default: return i8_kernel<4, ST, OT>();
+        case 1: return i8_kernel<1, false, ST, OT>();
+        case 2: return i8_kernel<2, false, ST, OT>();
+        case 3: return i8_kernel<3, false, ST, OT>();
+        default: return i8_kernel<4, false, ST, OT>();
     }
 }
 
@@ -562,8 +654,18 @@ std::pair<I8Fn, int> pick_out(DType c, int NT) {
     return pick_nt<ST, float>(NT);
 }
 
+// Tiles of 4 token slots the kernel runs: fp32 activations (M <= 4) take two,
+// the token parts x_hi and x - x_hi.
+int i8_tiles(const GemmArgs& a) { return a.a_dtype == DType::F32 ? 2 : (a.M + kTokTile - 1) / kTokTile; }
+
 std::pair<I8Fn, int> select_i8(const GemmArgs& a) {
-    const int NT = (a.M + kTokTile - 1) / kTokTile;
+    if (a.a_dtype == DType::F32) {
+        // fp32 activations: fp32 output (hq_gemm's rule c_dtype == a_dtype or f32)
+        if (a.s_dtype == DType::F16) return i8_kernel<2, true, __half, float>();
+        if (a.s_dtype == DType::BF16) return i8_kernel<2, true, __nv_bfloat16, float>();
+        return i8_kernel<2, true, float, float>();
+    }
+    const int NT = i8_tiles(a);
     if (a.s_dtype == DType::F16) return pick_out<__half>(a.c_dtype, NT);
     if (a.s_dtype == DType::BF16) return pick_out<__nv_bfloat16>(a.c_dtype, NT);
     return pick_out<float>(a.c_dtype, NT);
@@ -591,13 +693,23 @@ size_t xscale_bytes(int K) { return ((size_t)(K / kBlockK) * 64 + 255) & ~(size_
 }  // namespace
 
 bool decode_i8_supported(const GemmArgs& a) {
-    if (a.wbits != 4 || a.bias || a.M < 1 || a.M > 16) return false;
-    if (a.a_dtype != DType::F16 && a.a_dtype != DType::BF16) return false;
+    if (a.wbits != 4 || a.M < 1 || a.M > 16) return false;
+    if (a.a_dtype == DType::F32) {
+        if (a.M > 4 || a.c_dtype != DType::F32) return false;
+    } else if (a.a_dtype != DType::F16 && a.a_dtype != DType::BF16) {
+        return false;
+    }
     if (a.c_dtype != a.a_dtype && a.c_dtype != DType::F32) return false;
+    // The reference form: fp32 scales and biases, with f16 or f32 activations (the same
+    // combinations the cluster split-K kernel takes).
+    if (a.bias && (a.s_dtype != DType::F32 || a.a_dtype == DType::BF16)) return false;
     return a.group % kBlockK == 0 && a.K % a.group == 0;
 }
 
-size_t decode_i8_workspace_bytes(int N, int K, int dev) { return split_bytes(N, K, dev) + pieces_bytes(K) + xscale_bytes(K); }
+// split state, activation pieces, x scales, x sums
+size_t decode_i8_workspace_bytes(int N, int K, int dev) {
+    return split_bytes(N, K, dev) + pieces_bytes(K) + 2 * xscale_bytes(K);
+}
 
 cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     int dev = 0;
@@ -605,9 +717,10 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     if (e != cudaSuccess) return e;
     const size_t split = split_bytes(a.N, a.K, dev);
     if (!a.ws || a.ws_bytes < decode_i8_workspace_bytes(a.N, a.K, dev)) return cudaErrorInvalidValue;
-    const int NT = (a.M + kTokTile - 1) / kTokTile;
+    const int NT = i8_tiles(a);
     int8_t* pieces = reinterpret_cast<int8_t*>(a.ws + split);
     float* xscale = reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K));
+    float* xsum = a.bias ? reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K) + xscale_bytes(a.K)) : nullptr;
 
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -621,11 +734,14 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     pc.attrs = pdl;
     pc.numAttrs = 1;
     if (a.a_dtype == DType::F16)
-        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__half>, static_cast<const __half*>(a.A), a.M, a.K, a.group,
-                               NT * kTokTile, pieces, xscale);
+        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__half, false>, static_cast<const __half*>(a.A), a.M, a.K, a.group,
+                               NT * kTokTile, pieces, xscale, xsum);
+    else if (a.a_dtype == DType::BF16)
+        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__nv_bfloat16, false>, static_cast<const __nv_bfloat16*>(a.A), a.M,
+                               a.K, a.group, NT * kTokTile, pieces, xscale, xsum);
     else
-        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(a.A), a.M, a.K,
-                               a.group, NT * kTokTile, pieces, xscale);
+        e = cudaLaunchKernelEx(&pc, x_prep_kernel<float, true>, static_cast<const float*>(a.A), a.M, a.K, a.group,
+                               NT * kTokTile, pieces, xscale, xsum);
     if (e != cudaSuccess) return e;
 
     // 2. the GEMM
@@ -636,8 +752,10 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     memset(&p, 0, sizeof p);
     p.W = a.W;
     p.S = a.S;
+    p.bias = a.bias;
     p.pieces = pieces;
     p.xscale = xscale;
+    p.xsum = xsum;
     p.C = a.C;
     p.err = device_error_word(dev);
     p.counters = reinterpret_cast<unsigned*>(a.ws);

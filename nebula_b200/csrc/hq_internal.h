@@ -85,6 +85,9 @@ cudaError_t launch_tq1_0_to_tile_t2(const uint8_t* w, uint8_t* tile, uint16_t* s
 
 // Plain fp32 GEMM (the engine shim's forward_reference).
 cudaError_t launch_f32_gemm(const float* X, const float* W, float* Y, int M, int K, int N, cudaStream_t s);
+// Scalar int4 GEMM on the linear layout (the engine shim's forward_baseline_int4); B may be null.
+cudaError_t launch_baseline_u4(const float* X, const uint32_t* W, const float* S, const float* B, float* Y, int M,
+                               int K, int N, int group, cudaStream_t s);
 
 // Message returned by hq_last_error_string() on this host thread.
 void set_last_error(const char* msg);

@@ -3,7 +3,10 @@
 //
 // Mirrors hydrogen/src/model/marlin_gemm.cu:381-758 method by method; the
 // kernels are this library's (decode / tensor-core), the fp32 check GEMM is the
-// bit-compatible restatement of kernel_reference_gemm (hq_misc.cu).
+// bit-compatible restatement of kernel_reference_gemm (hq_misc.cu), and
+// forward_baseline_int4 is, as in the reference, an un-optimised scalar kernel
+// on the linear layout: the yardstick run_benchmark_sweep's speedup_ratio
+// measures forward_marlin_int4 against.
 #include "hq.h"
 #include "hq_internal.h"
 #include "hq_layout.h"
@@ -81,7 +84,10 @@ MarlinRepackResult MarlinGemmEngine::repack_q4k_to_marlin(const uint8_t* h_src_q
 
 void MarlinGemmEngine::forward_baseline_int4(const float* d_X, const uint32_t* d_W_linear, const float* d_scales,
                                              const float* d_biases, float* d_Y, uint32_t M) {
-    run(d_X, d_W_linear, HQ_WFMT_LINEAR_U4, d_scales, d_biases, d_Y, M);
+    if (!d_X || !d_W_linear || !d_scales || !d_Y) throw std::runtime_error("forward_baseline_int4: null pointer");
+    check_cuda(hq::launch_baseline_u4(d_X, d_W_linear, d_scales, d_biases, d_Y, (int)M, (int)config_.K,
+                                      (int)config_.N, (int)config_.group_size, nullptr),
+               "forward_baseline_int4 launch");
 }
 
 void MarlinGemmEngine::forward_marlin_int4(const float* d_X, const uint32_t* d_W_marlin, const float* d_scales,

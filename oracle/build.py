@@ -5,7 +5,10 @@
 * ``build_ref()`` compiles the reference's own sources where they lie (nothing is
   copied): ``hydrogen/src/model/marlin_gemm.cu`` with ``ref_shim.cu`` into
   ``oracle/_ref/libref_marlin.so``, and ``hydrogen/src/batcher/split_fuse.cpp``
-  with ``ref_batcher_shim.cpp`` into ``oracle/_ref/libref_batcher.so``.  It needs
+  with ``ref_batcher_shim.cpp`` into ``oracle/_ref/libref_batcher.so``.
+* ``build_ref_h08()`` compiles the reference's H08 harness
+  ``hydrogen/src/tools/bench_marlin_gemm.cpp`` against this library's drop-in
+  header and links it to ``nebula_b200/libhq.so``.  These need
   the reference tree: the directory named by ``HQ_REFERENCE_ROOT``, else a
   checkout named ``reference`` beside this repository.  Where neither exists
   (the GPU machine) the prebuilt libraries are used; they are kept out of
@@ -105,6 +108,30 @@ def build_ref_batcher(force: bool = False) -> str | None:
     return out
 
 
+def build_ref_h08(force: bool = False) -> str | None:
+    """Compile the reference's H08 harness, hydrogen/src/tools/bench_marlin_gemm.cpp, unmodified,
+    against this library's drop-in header (oracle/h08/marlin_gemm.hpp includes
+    include/hq_marlin_gemm.hpp) and link it to nebula_b200/libhq.so: the reference's acceptance
+    program for the MarlinGemmEngine API, run on the drop-in.  Output:
+    oracle/_ref/hydrogen_bench_marlin_gemm (rpath to the in-tree libhq.so).  None when the
+    reference tree or libhq.so is absent and no prebuilt harness exists."""
+    out = os.path.join(HERE, "_ref", "hydrogen_bench_marlin_gemm")
+    src = os.path.join(ref_root(), "hydrogen", "src", "tools", "bench_marlin_gemm.cpp")
+    lib = os.path.join(ROOT, "nebula_b200", "libhq.so")
+    hdrs = [os.path.join(HERE, "h08", "marlin_gemm.hpp"), os.path.join(ROOT, "include", "hq_marlin_gemm.hpp")]
+    if not (os.path.exists(src) and os.path.exists(lib)):
+        return out if os.path.exists(out) else None
+    if force or _stale(out, [src, lib, __file__] + hdrs):
+        os.makedirs(os.path.dirname(out), exist_ok=True)
+        cmd = ["g++", "-std=c++20", "-O2", "-I", os.path.join(HERE, "h08"), "-I", os.path.join(ROOT, "include"),
+               src, "-o", out + ".tmp", "-L", os.path.dirname(lib), "-lhq",
+               "-Wl,-rpath,$ORIGIN/../../nebula_b200"]
+        subprocess.run(cmd, check=True)
+        os.replace(out + ".tmp", out)
+    return out
+
+
 if __name__ == "__main__":
     print(build_oracle(force="--force" in sys.argv))
     print(build_ref(force="--force" in sys.argv))
+    print(build_ref_h08(force="--force" in sys.argv))

@@ -50,8 +50,8 @@ def ref_lib():
         _ref.ref_engine_destroy.argtypes = [c_void_p]
         for f in ("ref_forward_reference", "ref_forward_marlin", "ref_forward_baseline", "ref_forward_cutlass_int8"):
             getattr(_ref, f).restype = c_int
-        _ref.ref_repack_q4k_to_marlin.argtypes = [c_void_p, c_void_p, ctypes.c_uint32,
-                                                  ctypes.c_uint32, ctypes.POINTER(c_double)]
+        _ref.ref_engine_repack_q4k_to_marlin.argtypes = [c_void_p, c_void_p, c_void_p, ctypes.c_uint32,
+                                                         ctypes.c_uint32, ctypes.POINTER(c_double)]
     return _ref
 
 
@@ -296,13 +296,22 @@ def max_rel_err(y, y_ref) -> float:
 # ----------------------------------------------------- reference (compiled)
 
 def ref_repack_q4k_to_marlin(linear: np.ndarray, K: int, N: int):
-    """Run the reference's own repack (marlin_gemm.cu:432-467) on the CPU."""
+    """Run the reference's own repack (marlin_gemm.cu:432-467) through a constructed
+    MarlinGemmEngine.  The engine's constructor allocates device memory, so this needs a
+    GPU; returns None when the reference library is absent or no engine can be built."""
     r = ref_lib()
     if r is None:
         return None
-    out = np.zeros((K // 32, N, 4), np.uint32)
-    ms = c_double(0.0)
-    rc = r.ref_repack_q4k_to_marlin(_p(np.ascontiguousarray(linear, np.uint32)), _p(out), K, N, ctypes.byref(ms))
-    if rc != 0:
-        raise RuntimeError(r.ref_last_error().decode())
-    return out
+    eng = r.ref_engine_create(1, K, N, 32)
+    if not eng:
+        return None
+    try:
+        out = np.zeros((K // 32, N, 4), np.uint32)
+        ms = c_double(0.0)
+        rc = r.ref_engine_repack_q4k_to_marlin(c_void_p(eng), _p(np.ascontiguousarray(linear, np.uint32)), _p(out),
+                                               K, N, ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError(r.ref_last_error().decode())
+        return out
+    finally:
+        r.ref_engine_destroy(c_void_p(eng))

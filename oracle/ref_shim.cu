@@ -2,16 +2,15 @@
 //
 // TEST INFRASTRUCTURE ONLY.  Linked with the reference's unmodified
 // hydrogen/src/model/marlin_gemm.cu (compiled where it lies) into
-// oracle/_ref/libref_marlin.so so that tests can (a) run the reference's host
-// repack on the CPU and (b) run the reference's kernel_reference_gemm and
-// Marlin kernel on a B200 against this project's oracle.  Exceptions thrown by
+// oracle/_ref/libref_marlin.so so that tests can run the reference's host
+// repack, its kernel_reference_gemm and its Marlin kernel on a B200 against
+// this project's oracle.  Every entry point works on a constructed engine.  Exceptions thrown by
 // the reference (CUDA_CHECK, marlin_gemm.cu:19-27) become return code -1.
 #include "marlin_gemm.hpp"
 
 #include <cstdint>
 #include <cstring>
 #include <exception>
-#include <new>
 
 namespace {
 char g_err[512];
@@ -25,23 +24,18 @@ extern "C" {
 
 const char* ref_last_error() { return g_err; }
 
-// MarlinGemmEngine::repack_q4k_to_marlin (marlin_gemm.cu:432-467) reads and
-// writes only its arguments.  Constructing an engine allocates device memory
-// (:381-385, :391-416), which is impossible without a GPU, so the member is
-// invoked on raw storage of the right size and alignment: the function never
-// touches the object, which is why this is sound in practice on this
-// compiler even though the object is not constructed.
-int ref_repack_q4k_to_marlin(const uint32_t* src, uint32_t* dst, uint32_t K, uint32_t N,
-                             double* ms_out) {
+// MarlinGemmEngine::repack_q4k_to_marlin (marlin_gemm.cu:432-467) called on a
+// constructed engine (ref_engine_create).  The constructor allocates device
+// memory (:381-385, :391-416), so this needs a GPU.
+int ref_engine_repack_q4k_to_marlin(void* e, const uint32_t* src, uint32_t* dst, uint32_t K, uint32_t N,
+                                    double* ms_out) {
     try {
-        alignas(hydrogen::MarlinGemmEngine) static unsigned char storage[sizeof(hydrogen::MarlinGemmEngine)];
-        auto* eng = reinterpret_cast<hydrogen::MarlinGemmEngine*>(storage);
-        hydrogen::MarlinRepackResult r =
-            eng->repack_q4k_to_marlin(reinterpret_cast<const uint8_t*>(src), dst, K, N);
+        hydrogen::MarlinRepackResult r = static_cast<hydrogen::MarlinGemmEngine*>(e)->repack_q4k_to_marlin(
+            reinterpret_cast<const uint8_t*>(src), dst, K, N);
         if (ms_out) *ms_out = r.repack_time_ms;
         return 0;
-    } catch (const std::exception& e) {
-        set_err(e.what());
+    } catch (const std::exception& ex) {
+        set_err(ex.what());
         return -1;
     }
 }

@@ -1,16 +1,19 @@
 """Generate the committed golden fixtures (tests/golden/*.npz).
 
-Run in the build container (it needs oracle/liboracle.so and, for the reference
-columns, oracle/_ref/libref_marlin.so compiled from the reference source):
+Needs oracle/liboracle.so and, for the reference columns, oracle/_ref/libref_marlin.so
+compiled from the reference source (both built by __graft_entry__.build()), on a machine
+with a GPU: the reference repack runs on a constructed MarlinGemmEngine, whose
+constructor allocates device memory.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py           # (re)write golden.npz
+    python tests/golden/make_golden.py --check   # regenerate in memory, compare with golden.npz
 
 Contents
   * int4 / ternary / TQ1_0 cases at small and ragged shapes: the seeded inputs,
     every packed layout, and the oracle's fp32 outputs;
   * ``*_ref_quad``: the Marlin-quad repack produced by the reference's own
     MarlinGemmEngine::repack_q4k_to_marlin (hydrogen/src/model/marlin_gemm.cu
-    :432-467) run here through oracle/_ref -- the vector that pins the oracle's
+    :432-467) run through oracle/_ref -- the vector that pins the oracle's
     restatement of that repack;
   * ``cfg0_*``: BASELINE config 0 (A fp16 [16,4096] ~N(0,1), int4 [4096,4096]
     g128, fp16 scales ~U(0.005,0.02), seed 0): input checksums and the oracle
@@ -42,7 +45,7 @@ def int4_case(prefix, M, K, N, group, seed, dtype, out):
     quad = o.repack_marlin_quad(lin, K, N)
     ref_quad = o.ref_repack_q4k_to_marlin(lin, K, N)
     if ref_quad is None:
-        raise SystemExit("oracle/_ref/libref_marlin.so is missing: run python oracle/build.py first")
+        raise SystemExit("no reference engine: oracle/_ref/libref_marlin.so is missing or no GPU is visible")
     assert np.array_equal(quad, ref_quad), "oracle repack differs from the reference repack"
     tile = o.pack_tile(q, 4)
     Y = o.w4_gemm(A, lin, S, None, group=group, nthreads=1)
@@ -119,8 +122,17 @@ def main():
     Y = o.w4_gemm(A, lin, S, None, group=128)
     out["cfg0_Y"] = Y
     out["cfg0_sha"] = np.array([sha(A), sha(lin), sha(S)])
-    np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
-    print("wrote", os.path.join(HERE, "golden.npz"), sum(v.nbytes for v in out.values()), "bytes raw")
+    path = os.path.join(HERE, "golden.npz")
+    if "--check" in sys.argv[1:]:
+        old = np.load(path)
+        def same(a, b):  # byte equality, so NaN outputs compare equal to themselves
+            return a.dtype == b.dtype and a.shape == b.shape and a.tobytes() == b.tobytes()
+        bad = sorted(k for k in set(old.files) | set(out) if k not in old.files or k not in out
+                     or not same(old[k], np.asarray(out[k])))
+        print("golden.npz reproduced: " + ("yes" if not bad else "NO, differs in " + ", ".join(bad)))
+        raise SystemExit(1 if bad else 0)
+    np.savez_compressed(path, **out)
+    print("wrote", path, sum(v.nbytes for v in out.values()), "bytes raw")
 
 
 if __name__ == "__main__":

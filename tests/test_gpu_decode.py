@@ -142,11 +142,12 @@ def test_decode_ternary_parity(K, N, M, dtype):
     assert o.max_rel_err(y, ref) <= TOL[dtype]
 
 
-def test_f32_activations_with_bias_match_reference_semantics():
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_f32_activations_with_bias_match_reference_semantics(M):
     """The reference's own form: fp32 X, fp32 scale and bias, w = u*s + b (marlin_gemm.cu:208-209),
     with its synthetic distributions (:470-487) and its acceptance bound max_abs_error < 1e-3."""
     rng = np.random.default_rng(42)
-    M, K, N, g = 8, 4096, 4096, 128
+    K, N, g = 4096, 4096, 128
     X = (rng.standard_normal((M, K)) * 0.25).astype(np.float32)
     S = (0.05 + rng.integers(0, 1000, size=(K // g, N)) * 1e-4).astype(np.float32)
     B = (-8.0 * S).astype(np.float32)
@@ -159,6 +160,64 @@ def test_f32_activations_with_bias_match_reference_semantics():
     y2 = run_gemm(X, cuda(quad, None), S, N, g, "f32", wfmt=_lib.HQ_WFMT_MARLIN_QUAD)  # symmetric form
     ref2 = o.w4_gemm(X, lin, S, None, group=g)
     assert np.max(np.abs(y2 - ref2)) < 1e-3
+
+
+@pytest.mark.parametrize("K,N,g", [(256, 48, 128), (4096, 4096, 128), (262144, 144, 64), (180224, 272, 256),
+                                   (17408, 5120, 128), (5120, 34816, 128)])
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_f32_activations_integer_path(K, N, g, M, with_bias):
+    """fp32 X at M <= 4.  Layers of >= 8192 (strip group, k-block) units run the integer-MMA
+    stream kernel with each activation held as two fixed-point parts (30 bits) and, with a bias,
+    the (8 s + b) * sum(x) term per scale group: ragged widths (N % 128 != 0) with group 64 / 256,
+    and the 27B down / gate_up shapes, whose scale groups straddle CTAs.  The two smaller
+    shapes run the cluster split-K kernel (two fp16 terms)."""
+    rng = np.random.default_rng(K + N + M + (7 if with_bias else 0))
+    X = (rng.standard_normal((M, K)) * 0.25).astype(np.float32)
+    X[0, :5] *= 40.0  # one large-magnitude group: the rest of the group keeps its bits in the second part
+    S = (0.05 + rng.integers(0, 1000, size=(K // g, N)) * 1e-4).astype(np.float32)
+    B = (-8.0 * S + 0.01 * rng.standard_normal(S.shape)).astype(np.float32) if with_bias else None
+    q = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    lin = o.pack_linear_u4(q)
+    ref = o.w4_gemm(X, lin, S, B, group=g)
+    y = run_gemm(X, cuda(o.pack_tile(q, 4), None), S, N, g, "f32", bias=B)
+    assert o.max_rel_err(y, ref) <= TOL["f32"]
+    y2 = run_gemm(X, cuda(o.pack_tile(q, 4), None), S, N, g, "f32", bias=B)
+    assert np.array_equal(y, y2)  # deterministic
+
+
+@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("dtype", ["f16"])
+def test_16bit_activations_with_fp32_scales_and_bias_wide_layer(M, dtype):
+    """fp16 X with the reference's fp32 scale and bias on a layer wide enough (>= 128 strip groups)
+    for the integer-MMA kernel; fp32 and fp16 outputs.  (A bias goes with f16 or f32 activations,
+    as hq.h states.)"""
+    K, N, g = 512, 16384, 128
+    rng = np.random.default_rng(M)
+    A, q, _ = o.gen_int4_case(M, K, N, group=g, seed=M + 5, a_dtype=dtype)
+    S = (0.05 + rng.integers(0, 1000, size=(K // g, N)) * 1e-4).astype(np.float32)
+    B = (-8.0 * S + 0.01 * rng.standard_normal(S.shape)).astype(np.float32)
+    lin = o.pack_linear_u4(q)
+    ref = o.w4_gemm(A, lin, S, B, group=g)
+    W = cuda(o.pack_tile(q, 4), None)
+    y32 = run_gemm(A, W, S, N, g, dtype, bias=B, s_dtype="f32", out_dtype=torch.float32)
+    assert o.max_rel_err(y32, ref) <= 1e-4
+    y16 = run_gemm(A, W, S, N, g, dtype, bias=B, s_dtype="f32")
+    assert o.max_rel_err(y16, ref) <= TOL[dtype]
+
+
+def test_f32_activations_nan_group_poisons_only_its_token():
+    """A scale group of fp32 activations holding NaN makes that token's outputs NaN, others finite."""
+    M, K, N, g = 3, 1024, 272, 128
+    rng = np.random.default_rng(3)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    X[1, 300] = np.nan
+    S = (0.05 + rng.integers(0, 1000, size=(K // g, N)) * 1e-4).astype(np.float32)
+    q = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    y = run_gemm(X, cuda(o.pack_tile(q, 4), None), S, N, g, "f32")
+    assert np.all(np.isnan(y[1])) and np.all(np.isfinite(y[[0, 2]]))
+    ref = o.w4_gemm(X[[0, 2]], o.pack_linear_u4(q), S, None, group=g)
+    assert o.max_rel_err(y[[0, 2]], ref) <= TOL["f32"]
 
 
 @pytest.mark.parametrize("K,N", [(64, 16), (512, 144), (5120, 7168)])

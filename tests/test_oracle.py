@@ -20,24 +20,29 @@ def golden():
 
 # ----------------------------------------------------------- reference pins
 
+@pytest.mark.gpu
 def test_repack_matches_reference_binary_random():
-    """Oracle repack == MarlinGemmEngine::repack_q4k_to_marlin (marlin_gemm.cu:432-467) on random words."""
+    """Oracle repack == MarlinGemmEngine::repack_q4k_to_marlin (marlin_gemm.cu:432-467) on random words
+    and on benchmark_repacking's constant fill (:648), through a constructed reference engine (its
+    constructor allocates device memory, hence the GPU)."""
     if o.ref_lib() is None:
-        pytest.skip("reference library not built here (no reference tree)")
+        pytest.skip("reference library not built (no reference tree at build time)")
     rng = np.random.default_rng(5)
     for K, N in [(32, 1), (64, 3), (512, 40), (4096, 64)]:
         lin = rng.integers(0, 2**32, size=(K // 8, N), dtype=np.uint64).astype(np.uint32)
-        assert np.array_equal(o.repack_marlin_quad(lin, K, N), o.ref_repack_q4k_to_marlin(lin, K, N))
+        ref = o.ref_repack_q4k_to_marlin(lin, K, N)
+        assert ref is not None, o.ref_lib().ref_last_error().decode()
+        assert np.array_equal(o.repack_marlin_quad(lin, K, N), ref)
+    K, N = 4096, 64
+    lin = np.full((K // 8, N), 0x12345678, np.uint32)
+    assert np.array_equal(o.repack_marlin_quad(lin, K, N), o.ref_repack_q4k_to_marlin(lin, K, N))
 
 
 def test_repack_kat_constant_fill():
     """benchmark_repacking's constant fill (marlin_gemm.cu:648): every output word is the input word."""
     K, N = 4096, 64
     lin = np.full((K // 8, N), 0x12345678, np.uint32)
-    quad = o.repack_marlin_quad(lin, K, N)
-    assert np.all(quad == 0x12345678)
-    if o.ref_lib() is not None:
-        assert np.array_equal(quad, o.ref_repack_q4k_to_marlin(lin, K, N))
+    assert np.all(o.repack_marlin_quad(lin, K, N) == 0x12345678)
 
 
 def test_golden_reference_repack_vectors(golden):
