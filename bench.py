@@ -742,7 +742,10 @@ def main():
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")
-    ap.add_argument("--ar-ctas", type=int, default=128, help="CTAs of hq_allreduce_sum")
+    ap.add_argument("--ar-ctas", type=int, default=128, help="CTAs of hq_allreduce_sum in the TP stack")
+    ap.add_argument("--sweep-comm", default="hq", choices=["hq", "nccl"],
+                    help="all-reduce of the row-parallel outputs in the tensor-parallel decode sweep")
+    ap.add_argument("--sweep-ar-ctas", type=int, default=16, help="CTAs of hq_allreduce_sum in the decode sweep")
     ap.add_argument("--no-nvls", dest="nvls", action="store_false", help="hq_allreduce_sum without NVLink multicast")
     ap.add_argument("--prefill-ms", default="512,2048,8192", help="token counts of the prefill sweep")
     args = ap.parse_args()
@@ -799,6 +802,39 @@ def main():
     import ctypes
     vp = ctypes.c_void_p
 
+    # Tensor-parallel runs: the row-parallel (O, down) outputs are summed over the ranks
+    # after each GEMM, by hq_allreduce_sum on PyTorch symmetric memory (epoch 0: the call
+    # count lives in the flag area, so the calls replay inside the step's CUDA graph),
+    # or by NCCL.
+    sweep_hq = world > 1 and args.sweep_comm == "hq"
+    ar_bufs = {}
+    if sweep_hq:
+        import torch.distributed._symmetric_memory as symm
+        ar_flags = symm.empty(32, dtype=torch.int32, device=dev)
+        ar_flags.zero_()
+        hf = symm.rendezvous(ar_flags, dist.group.WORLD)
+        ar_fptrs = (ctypes.c_void_p * world)(*hf.buffer_ptrs)
+        for M in MS:
+            for name, _, _ in SHAPES:
+                if name in ("o", "down"):
+                    buf = symm.empty((M, weights[name][1]), dtype=torch.float16, device=dev)
+                    hb = symm.rendezvous(buf, dist.group.WORLD)
+                    outs[M][name] = buf
+                    mc = int(hb.multicast_ptr or 0) if args.nvls else 0
+                    ar_bufs[(M, name)] = ((ctypes.c_void_p * world)(*hb.buffer_ptrs), hb, ctypes.c_void_p(mc))
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    def sweep_all_reduce(M, name, C):
+        if sweep_hq:
+            bp, _, mc = ar_bufs[(M, name)]
+            st = L.hq_allreduce_sum(bp, ar_fptrs, mc, world, rank, _lib.HQ_F16, C.numel(), 0, args.sweep_ar_ctas,
+                                    vp(sh))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        else:
+            dist.all_reduce(C)
+
     def launch(name, M, copy, stream_handle, A=None, C=None):
         Kl, Nl, copies = weights[name]
         W, S = copies[copy]
@@ -825,7 +861,7 @@ def main():
             if timing_events is not None:
                 timing_events[i][1].record(stream)
             if ar:
-                dist.all_reduce(C)
+                sweep_all_reduce(M, name, C)
 
     # warm-up (also sets kernel attributes before graph capture)
     with torch.cuda.stream(stream):
@@ -918,7 +954,7 @@ def main():
             acts[M][name].copy_(hostA[M][name], non_blocking=True)
             C = launch(name, M, copy_of(M), sh)
             if ar:
-                dist.all_reduce(C)
+                sweep_all_reduce(M, name, C)
             hostC[M][name].copy_(C, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -992,6 +1028,10 @@ def main():
             "config": {"workload": "decode_sweep (BASELINE configs[1]): 27B layer QKV 5120x7168, O 5120x5120, "
                                    "gate_up 5120x34816, down 17408x5120 at M in {1,2,4,8,16}; int4 g128, fp16 A",
                        "global_batch": "M in {1,2,4,8,16}", "parallelism": f"tp{world}" if world > 1 else "single",
+                       "collective": None if world == 1 else (
+                           "NCCL all_reduce" if not sweep_hq else
+                           "hq_allreduce_sum, NVLS multicast" if any(v[2].value for v in ar_bufs.values())
+                           else "hq_allreduce_sum, NVLink peer loads"),
                        "l2": f"inputs larger than L2: {args.copies} weight copies per shape "
                              f"({args.copies * layer_bytes / 1e6:.0f} MB); the GEMM at the i-th M reads copy i, so "
                              "every GEMM of a step reads weights no other GEMM of the step touched",

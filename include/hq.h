@@ -271,7 +271,10 @@ HQ_API hq_status hq_embedding_lookup(const void* table, int w_type, int token_id
  *                  it the switch sums (multimem.ld_reduce, fp32 accumulation)
  *                  and broadcasts (multimem.st): each rank moves 2/world of the
  *                  vector over NVLink instead of 2 (world-1)/world.
- *   epoch:         1 for the first call on these flags, +1 for every call after.
+ *   epoch:         1 for the first call on these flags, +1 for every call after;
+ *                  or 0 on every call: the kernel then takes the same number
+ *                  from a call counter in the flag area, so the call can be
+ *                  captured in a CUDA graph and replayed.
  *   ctas:          CTAs per call (the same on every call with these flags).
  * Every rank makes the same calls in the same order on its own stream; on
  * return every buffer holds the sum (fp32 accumulation; every rank holds the

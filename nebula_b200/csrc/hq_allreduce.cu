@@ -20,6 +20,9 @@
 //      way every rank ends with the same bits;
 //   3. barrier on slots [1][*] once all of this rank's CTAs have pushed (a
 //      counter in the flag area picks the last CTA): every slice has arrived.
+// The epoch of a call is either passed in or, with epoch 0, read from that
+// counter (it grows by the CTA count per call), so a call can be captured in a
+// CUDA graph and replayed.
 // Every wait is bounded (kWaitBudgetNs): on time-out the kernel records
 // kDevTimeout in the device error word and returns; the result is then
 // undefined but no GPU is left spinning.
@@ -114,14 +117,23 @@ struct ArParams {
 template <typename T>
 __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const __grid_constant__ ArParams p) {
     __shared__ int s_ok;
+    __shared__ unsigned s_epoch;
     unsigned* my_flags = p.flags[p.rank];
+    unsigned* counter = my_flags + 2 * kArMaxWorld;
+    // 0. the epoch: given, or derived from this rank's CTA arrival counter, which
+    // every earlier call on these flags (same CTA count) raised by gridDim.x, and
+    // which CTAs of this call raise only after step 1 (fewer than gridDim.x of
+    // them before any CTA of this call reads it): epoch = counter / CTAs + 1.
+    if (threadIdx.x == 0) s_epoch = p.epoch ? p.epoch : atomicAdd(counter, 0u) / gridDim.x + 1u;
+    __syncthreads();
+    const unsigned epoch = s_epoch;
     // 1. every partial is written (each rank's previous kernels have finished)
     if (threadIdx.x == 0) {
         if (blockIdx.x == 0) {
             __threadfence_system();
-            for (int j = 0; j < p.world; ++j) st_release_sys(p.flags[j] + 0 * kArMaxWorld + p.rank, p.epoch);
+            for (int j = 0; j < p.world; ++j) st_release_sys(p.flags[j] + 0 * kArMaxWorld + p.rank, epoch);
         }
-        s_ok = wait_all(my_flags, 0, p.world, p.epoch, p.err) ? 1 : 0;
+        s_ok = wait_all(my_flags, 0, p.world, epoch, p.err) ? 1 : 0;
     }
     __syncthreads();
 
@@ -184,13 +196,12 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const __grid_cons
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        unsigned* counter = my_flags + 2 * kArMaxWorld;
         const unsigned done = atomicAdd(counter, 1u) + 1u;
-        if (done == p.epoch * gridDim.x) {  // every CTA's pushes are ordered before this point
+        if (done == epoch * gridDim.x) {  // every CTA's pushes are ordered before this point
             __threadfence_system();
-            for (int j = 0; j < p.world; ++j) st_release_sys(p.flags[j] + 1 * kArMaxWorld + p.rank, p.epoch);
+            for (int j = 0; j < p.world; ++j) st_release_sys(p.flags[j] + 1 * kArMaxWorld + p.rank, epoch);
         }
-        if (s_ok) wait_all(my_flags, 1, p.world, p.epoch, p.err);
+        if (s_ok) wait_all(my_flags, 1, p.world, epoch, p.err);
     }
 }
 
@@ -202,8 +213,8 @@ extern "C" HQ_API hq_status hq_allreduce_sum(void* const* peer_bufs, unsigned* c
                                              int world, int rank, hq_dtype dtype, size_t count, unsigned epoch,
                                              int ctas, hq_stream_t stream) {
     using namespace hq;
-    if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world || !peer_bufs || !peer_flags || epoch == 0 ||
-        ctas < 1 || ctas > 1024) {
+    if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world || !peer_bufs || !peer_flags || ctas < 1 ||
+        ctas > 1024) {
         set_last_error("hq_allreduce_sum: bad world/rank/pointers/epoch/ctas");
         return HQ_ERR_INVALID_ARG;
     }

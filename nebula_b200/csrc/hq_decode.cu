@@ -639,9 +639,17 @@ int cluster_size(const void* fn, int smem, int N, int K, int wbits, int dev) {
 bool g_early_weights = true;
 
 // Smallest layer the integer-MMA stream kernel takes: in strip groups of 128
-// columns for 16-bit activations, in (strip group, k-block) units for fp32.
+// columns for 16-bit activations, in (strip group, k-block) units for fp32; and
+// its largest M (one tile of 4 token slots: at M = 8 the cluster kernel is
+// faster, gate_up 27.8 us against 28.4).  The tcgen05 kernel's narrowest layer.
 #ifndef HQ_DECODE_I8_MIN_NSG
 #define HQ_DECODE_I8_MIN_NSG 128
+#endif
+#ifndef HQ_DECODE_I8_MAX_M
+#define HQ_DECODE_I8_MAX_M 4
+#endif
+#ifndef HQ_DECODE_TC_MIN_NSG
+#define HQ_DECODE_TC_MIN_NSG 128
 #endif
 #ifndef HQ_DECODE_I8_MIN_UNITS_F32
 #define HQ_DECODE_I8_MIN_UNITS_F32 8192
@@ -676,11 +684,12 @@ cudaError_t launch_decode(const GemmArgs& a) {
     const TileGeom tg(a.K, a.N, a.wbits);
     const bool i8_shape = a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
                                                   : tg.NSG >= HQ_DECODE_I8_MIN_NSG;
-    if (a.M <= 4 && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
-    // M > 8 on wide layers runs on tcgen05: the mma.sync kernel needs two token
-    // tiles there and the tensor-memory kernel's cost does not depend on M.
-    // Narrow layers (few strip groups) and M <= 8 stream faster here.
-    if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= 48 && decode_tc_supported(a))
+    if (a.M <= HQ_DECODE_I8_MAX_M && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
+    // M > 8 on wide layers (>= 128 strip groups) runs on tcgen05: the mma.sync
+    // kernel needs two token tiles there and the tensor-memory kernel's cost does
+    // not depend on M (gate_up at M = 16: 34.1 us against 47.1).  Narrower
+    // layers stream faster here (QKV at M = 16: 15.2 us against 17.2).
+    if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= HQ_DECODE_TC_MIN_NSG && decode_tc_supported(a))
         return launch_decode_tc(a, g_early_weights);
     const TileGeom geo(a.K, a.N, a.wbits);
     const KernelInfo ki = select_kernel(a);

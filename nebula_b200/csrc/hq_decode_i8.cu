@@ -1,4 +1,4 @@
-// hq_decode_i8.cu -- decode GEMM (M <= 16) on the integer tensor cores:
+// hq_decode_i8.cu -- decode GEMM (M <= 8) on the integer tensor cores:
 // int4 codes x fp16/bf16 activations through mma.sync s8 x s8 -> s32.
 //
 // Replaces, for int4 weights, 16-bit activations and no bias, the reference's
@@ -67,6 +67,9 @@
 #ifndef HQ_DECODE_I8_PRODUCERS
 #define HQ_DECODE_I8_PRODUCERS 2
 #endif
+#ifndef HQ_DECODE_I8_UPS
+#define HQ_DECODE_I8_UPS 8
+#endif
 
 
 namespace hq {
@@ -79,7 +82,7 @@ constexpr int kProducerWarps = HQ_DECODE_I8_PRODUCERS;  // warp kNC issues the c
 static_assert(kNC == 8 || kNC == 16, "one or two consumer warps per strip");
 constexpr int kProducerWarp = kNC;
 constexpr int kThreads = (kNC + kProducerWarps) * 32;
-constexpr int kUPS = 8;        // k-blocks per stage (32 KB of full-group codes: one bulk copy)
+constexpr int kUPS = HQ_DECODE_I8_UPS;  // k-blocks per stage (4 KB of full-group codes each: one bulk copy)
 constexpr int kBatch = 4;      // k-blocks a consumer warp keeps in flight
 constexpr int kTokTile = 4;    // tokens per MMA n-tile (two pieces each)
 constexpr int kTileBytes = 512;  // piece bytes of one k-block and one 4-token tile
@@ -305,6 +308,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
     const int G = (int)gridDim.x, c = (int)blockIdx.x;
     const long long u_begin = range_begin(U, G, c), u_end = range_begin(U, G, c + 1);
     const int upg = p.group / kBlockK;  // k-blocks per scale group
+    // Scale group of a k-block: a shift for the usual power-of-two groups (64,
+    // 128, 256), a division otherwise (the branch is uniform).
+    const int upg_sh = (upg & (upg - 1)) == 0 ? __ffs(upg) - 1 : -1;
+    auto grp = [upg, upg_sh](int kb) { return upg_sh >= 0 ? kb >> upg_sh : kb / upg; };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -333,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             const int width = geo.width(d.sg);
             const int s_chunks = width * kStripCols * (int)sizeof(ST) / 16;  // 16-byte pieces of one scale row
             const uint32_t wbytes = (uint32_t)d.n * (uint32_t)width * 512u;
-            const int g_first = d.kb / upg, ng = (d.kb + d.n - 1) / upg - g_first + 1;
+            const int g_first = grp(d.kb), ng = grp(d.kb + d.n - 1) - g_first + 1;
             if (pl == 0) {
                 mbar_arrive_expect_tx(&full[slot], wbytes);
                 bulk_g2s_hint(st, p.W + geo.unit_offset((long long)d.sg * KB + d.kb), wbytes, &full[slot], pol);
@@ -353,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
         auto issue_x = [&](int it, const Span& d) {
             const int slot = it % kStages;
             uint8_t* st = stage_ptr(it);
-            const int g_first = d.kb / upg, ng = (d.kb + d.n - 1) / upg - g_first + 1;
+            const int g_first = grp(d.kb), ng = grp(d.kb + d.n - 1) - g_first + 1;
             const int p_chunks = d.n * NT * kTileBytes / 16;
             const int8_t* psrc = p.pieces + (size_t)d.kb * NT * kTileBytes;
             for (int i = pl; i < p_chunks; i += 32 * kProducerWarps) cp_async16(st + L::kX + 16 * i, psrc + 16 * i);
@@ -540,9 +547,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
         if (sl < width && bn > 0) {
             const uint32_t unit_bytes = (uint32_t)width * 512u;
             const uint8_t* wbase = stage + (b0 * (int)unit_bytes) + sl * 512 + lane * 16;
-            const int g_stage = d.kb / upg;
-            int gl = (d.kb + b0) / upg - g_stage;                     // scale row of k-block b0
-            int gend = ((d.kb + b0) / upg + 1) * upg - (d.kb + b0);  // k-blocks of the batch to its group's end
+            const int g_stage = grp(d.kb);
+            const int g_b0 = grp(d.kb + b0);
+            int gl = g_b0 - g_stage;                     // scale row of k-block b0
+            int gend = (g_b0 + 1) * upg - (d.kb + b0);  // k-blocks of the batch to its group's end
             uint4 wv[kBatch];
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
@@ -552,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             for (int u = 0; u < kBatch; ++u) {
                 if (u >= bn) break;
                 if constexpr (L::kBias)
-                    if (p.bias && (d.kb + b0 + u) % upg == 0) add_bias(stage, gl);
+                    if (p.bias && grp(d.kb + b0 + u) * upg == d.kb + b0 + u) add_bias(stage, gl);
                 const uint32_t l0 = q16_lo(wv[u].x), l1 = q16_lo(wv[u].z), l2 = q16_lo(wv[u].y), l3 = q16_lo(wv[u].w);
                 const uint32_t h0 = q16_hi(wv[u].x), h1 = q16_hi(wv[u].z), h2 = q16_hi(wv[u].y), h3 = q16_hi(wv[u].w);
 #pragma unroll
@@ -639,12 +647,7 @@ std::pair<I8Fn, int> i8_kernel() {
 
 template <typename ST, typename OT>
 std::pair<I8Fn, int> pick_nt(int NT) {
-    switch (NT) {
-        case 1: return i8_kernel<1, false, ST, OT>();
-        case 2: return i8_kernel<2, false, ST, OT>();
-        case 3: return i8_kernel<3, false, ST, OT>();
-        default: return i8_kernel<4, false, ST, OT>();
-    }
+    return NT == 1 ? i8_kernel<1, false, ST, OT>() : i8_kernel<2, false, ST, OT>();
 }
 
 template <typename ST>
@@ -693,7 +696,7 @@ size_t xscale_bytes(int K) { return ((size_t)(K / kBlockK) * 64 + 255) & ~(size_
 }  // namespace
 
 bool decode_i8_supported(const GemmArgs& a) {
-    if (a.wbits != 4 || a.M < 1 || a.M > 16) return false;
+    if (a.wbits != 4 || a.M < 1 || a.M > 8) return false;  // one or two tiles of 4 token slots
     if (a.a_dtype == DType::F32) {
         if (a.M > 4 || a.c_dtype != DType::F32) return false;
     } else if (a.a_dtype != DType::F16 && a.a_dtype != DType::BF16) {

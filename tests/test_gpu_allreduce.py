@@ -6,7 +6,8 @@ sums them in place.  Reference: the partials gathered with NCCL, summed in fp32
 in rank order and rounded once, which is exactly what the kernel computes, so
 the results are compared bit for bit, on every rank, over several calls in a row
 (each call a new epoch on the same flags), alternating the NVLS multicast path
-(when the GPUs support it) and the peer-load path.  Skipped when fewer than two
+(when the GPUs support it) and the peer-load path, then with epoch 0 inside a
+CUDA graph replayed five times.  Skipped when fewer than two
 GPUs are visible.  Peer-load path: bit for bit against the gathered fp32 sum.  NVLS
 path: the switch rounds its fp32 sum its own way (it differs from round-to-
 nearest in about a fifth of the elements), so within one ulp of the reference
@@ -91,6 +92,36 @@ def _worker(rank, port, out_dir):
                                             for o in others)))
                 dist.barrier()
                 del buf, hb
+        # epoch 0 (the kernel reads the call count from the flag area), captured in a CUDA
+        # graph with the copy of the partial and replayed: bit for bit on every replay.
+        n = 2304 * 64
+        buf = symm.empty(n, dtype=torch.bfloat16, device=dev)
+        hb = symm.rendezvous(buf, dist.group.WORLD)
+        bptrs = (ctypes.c_void_p * WORLD)(*hb.buffer_ptrs)
+        g = torch.Generator(device=dev)
+        g.manual_seed(777 + rank)
+        x = torch.randn(n, device=dev, generator=g).bfloat16()
+        parts = [torch.empty_like(x) for _ in range(WORLD)]
+        dist.all_gather(parts, x)
+        ref = sum(p_.float() for p_ in parts).bfloat16()
+        side = torch.cuda.Stream(device=dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            buf.copy_(x)
+            st = L.hq_allreduce_sum(bptrs, fptrs, None, WORLD, rank, _lib.HQ_BF16, n, 0, 64,
+                                    ctypes.c_void_p(side.cuda_stream))
+        assert st == 0, L.hq_last_error_string()
+        for _ in range(5):
+            dist.barrier()
+            gr.replay()
+            torch.cuda.synchronize()
+            assert L.hq_check_device_error() == 0
+            errs.append(int((buf.view(torch.int16) != ref.view(torch.int16)).sum().item()))
+        del gr
+        torch.cuda.synchronize()
+        dist.barrier()
         np.save(os.path.join(out_dir, f"mismatch_{rank}.npy"), np.array(errs))
     finally:
         dist.destroy_process_group()
