@@ -690,7 +690,7 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // not depend on M (gate_up at M = 16: 34.1 us against 47.1).  Narrower
     // layers stream faster here (QKV at M = 16: 15.2 us against 17.2).
     if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= HQ_DECODE_TC_MIN_NSG && decode_tc_supported(a))
-        return launch_decode_tc(a, g_early_weights);
+        return launch_decode_tc(a, false);
     const TileGeom geo(a.K, a.N, a.wbits);
     const KernelInfo ki = select_kernel(a);
     if (!ki.fn) return cudaErrorInvalidValue;
@@ -715,7 +715,12 @@ cudaError_t launch_decode(const GemmArgs& a) {
     p.group = a.group;
     p.err = device_error_word(dev);
     p.cs = cluster_size(reinterpret_cast<const void*>(ki.fn), ki.smem, a.N, a.K, a.wbits, dev);
-    p.early_weights = (g_early_weights && !a.weights_just_written) ? 1 : 0;
+    // Weights before griddepcontrol.wait only in the integer kernel: here the
+    // early copies compete with the previous kernel's tail and measured slower
+    // (27B down at M = 1: 18.6 us with them, 17.2 without; QKV 9.8 / 9.3; the
+    // tcgen05 kernel: gate_up at M = 16 34.2 / 33.7).  The launch itself still
+    // overlaps the previous kernel's tail (CTA start, barrier set-up).
+    p.early_weights = 0;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(geo.NSG * p.cs));
