@@ -645,6 +645,9 @@ bool g_early_weights = true;
 #ifndef HQ_DECODE_I8_MIN_NSG
 #define HQ_DECODE_I8_MIN_NSG 128
 #endif
+#ifndef HQ_DECODE_I8_MIN_NSG_T2
+#define HQ_DECODE_I8_MIN_NSG_T2 128
+#endif
 #ifndef HQ_DECODE_I8_MAX_M
 #define HQ_DECODE_I8_MAX_M 4
 #endif
@@ -661,10 +664,11 @@ void set_decode_launch_overlap(bool on) { g_early_weights = on; }
 
 bool decode_supported(const GemmArgs& a) { return select_kernel(a).fn != nullptr; }
 
-// Only the integer-MMA kernel (wide layers) keeps state in the workspace.
+// Only the integer-MMA kernel (wide layers, int4 or ternary) keeps state in the workspace.
 size_t decode_workspace_bytes(int M, int N, int K, int wbits, int dev) {
     (void)M;
-    return wbits == 4 ? decode_i8_workspace_bytes(N, K, dev) : 0;
+    (void)wbits;
+    return decode_i8_workspace_bytes(N, K, dev);
 }
 
 cudaError_t launch_decode(const GemmArgs& a) {
@@ -683,6 +687,7 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // twice the MMAs.  Smaller fp32 layers stay here (QKV 17.8 us against 19.4).
     const TileGeom tg(a.K, a.N, a.wbits);
     const bool i8_shape = a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
+                          : a.wbits == 2          ? tg.NSG >= HQ_DECODE_I8_MIN_NSG_T2
                                                   : tg.NSG >= HQ_DECODE_I8_MIN_NSG;
     if (a.M <= HQ_DECODE_I8_MAX_M && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
     // M > 8 on wide layers (>= 128 strip groups) runs on tcgen05: the mma.sync

@@ -98,10 +98,10 @@ constexpr int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi 
 // Stage layout.  With fp32 scales the stage also carries, per scale group, the
 // activation sums of the 16 token slots and the group's fp32 bias row (the
 // reference's u * s + b form; read only when the call has a bias).
-template <int NT, typename ST>
+template <int NT, int WB, typename ST>
 struct RingI8 {
     static constexpr bool kBias = std::is_same<ST, float>::value;
-    static constexpr int kW = kUPS * kGroupStrips * 512;  // codes
+    static constexpr int kW = kUPS * kGroupStrips * (WB == 4 ? 512 : 256);  // codes
     static constexpr int kXUnit = NT * kTileBytes;       // pieces of one k-block
     static constexpr int kX = kW;
     static constexpr int kSUnit = kGroupCols * (int)sizeof(ST);  // one scale row of the group's columns
@@ -109,7 +109,8 @@ struct RingI8 {
     static constexpr int kXS = kS + kUPS * kSUnit;  // x scales: 16 token slots x fp32 per scale group
     static constexpr int kXQ = kXS + kUPS * 64;     // x sums: 16 token slots x fp32 per scale group
     static constexpr int kB = kXQ + (kBias ? kUPS * 64 : 0);  // bias rows (fp32), as the scale rows
-    static constexpr int kBytes = align_up(kB + (kBias ? kUPS * kSUnit : 0), 128);
+    static constexpr int kXK = kB + (kBias ? kUPS * kSUnit : 0);  // ternary: x sums per (k-block, token slot), int
+    static constexpr int kBytes = align_up(kXK + (WB == 2 ? kUPS * 64 : 0), 128);
     static constexpr int kStages = clampi(kRingBudget / kBytes, 2, 8);
     static constexpr int kPair = kHalves > 1 ? 2 * 8 * NT * 32 * 8 : 0;  // two buffers of half 1's sums (float2 per lane)
     static constexpr int kSmem = kStages * kBytes + kPair + 128 + 2 * kStages * 8 + 16;
@@ -122,6 +123,7 @@ struct alignas(16) I8Params {
     const int8_t* pieces;  // [K/64][NT*4 tokens][2][4][16] (workspace)
     const float* xscale;   // [K/group][16] 2^-s per (group, token slot) (workspace)
     const float* xsum;     // [K/group][16] sum of x per (group, token slot) (workspace; read with a bias)
+    const int* xkb;        // ternary: [K/64][16] sum of the fixed-point x per (k-block, token slot) (workspace)
     void* C;
     unsigned* err;
     unsigned* counters;  // [NSG]
@@ -204,7 +206,8 @@ __device__ __forceinline__ void load8(const AT* p, float (&f)[8]) {
 template <typename AT, bool RES>
 __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restrict__ A, int M, int K, int group,
                                                               int slots, int8_t* __restrict__ pieces,
-                                                              float* __restrict__ xscale, float* __restrict__ xsum) {
+                                                              float* __restrict__ xscale, float* __restrict__ xsum,
+                                                              int* __restrict__ xkb) {
     if (threadIdx.x == 0) pdl_launch_dependents();
     // A may come from the previous kernel, and that kernel may still read the
     // pieces of the previous call.
@@ -284,14 +287,51 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
         ph[2 + hh] = hw[1];
         pl[hh] = lw[0];
         pl[2 + hh] = lw[1];
+        if (xkb) {  // ternary: sum of the fixed-point x over each k-block (8 octets = 8 lanes)
+            int sum8 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum8 += xf[i];
+            // the 8 lanes of an aligned octet group run this pass together (oct % 8 == 0)
+            const unsigned act = __activemask();
+#pragma unroll
+            for (int d = 4; d >= 1; d >>= 1) sum8 += __shfl_xor_sync(act, sum8, d);
+            if ((l16 & 7) == 0) xkb[(size_t)kb * 16 + m] = sum8;
+        }
     }
+}
+
+// Ternary codes c = q + 1 (2 bits, TILE_T2 word of 16 consecutive k of one
+// column, code e at field (e >> 1) + 8 (e & 1)) as u8 MMA operands in the k-slot
+// order of the int4 path (so the same activation pieces serve both):
+// MMA 0 takes e = {0,2,1,3} (slots 4t..) and 8 + {0,2,1,3} (slots 16 + 4t..),
+// MMA 1 takes e = {4,6,5,7} and 8 + {4,6,5,7}.  Four masks select fields
+// (f, f + 4, f + 8, f + 12) into bytes, four byte permutes pick the pairs.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ void t2_operands(uint32_t w, uint32_t& m0a, uint32_t& m0b, uint32_t& m1a, uint32_t& m1b) {
+    const uint32_t f0 = w & 0x03030303u, f1 = (w >> 2) & 0x03030303u;
+    const uint32_t f2 = (w >> 4) & 0x03030303u, f3 = (w >> 6) & 0x03030303u;
+    m0a = prmt(f0, f1, 0x6240u);
+    m0b = prmt(f0, f1, 0x7351u);
+    m1a = prmt(f2, f3, 0x6240u);
+    m1b = prmt(f2, f3, 0x7351u);
+}
+// D (16x8 s32) += A (16x32 u8) x B (32x8 s8).
+__device__ __forceinline__ void imma_16832_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // RES: fp32 activations in two slots per token (x_prep_kernel); tiles j and
 // j + NT/2 hold the two parts of the same tokens.
-template <int NT, bool RES, typename ST, typename OT>
+template <int NT, bool RES, int WB, typename ST, typename OT>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const __grid_constant__ I8Params p) {
-    using L = RingI8<NT, ST>;
+    using L = RingI8<NT, WB, ST>;
     constexpr int kStages = L::kStages;
 
     extern __shared__ uint8_t smem_raw[];
@@ -302,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
     volatile int* s_last = reinterpret_cast<volatile int*>(empty + kStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const TileGeom geo(p.K, p.N, 4);
+    const TileGeom geo(p.K, p.N, WB);
     const int KB = geo.KB;
     const long long U = geo.units();
     const int G = (int)gridDim.x, c = (int)blockIdx.x;
@@ -339,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             uint8_t* st = stage_ptr(it);
             const int width = geo.width(d.sg);
             const int s_chunks = width * kStripCols * (int)sizeof(ST) / 16;  // 16-byte pieces of one scale row
-            const uint32_t wbytes = (uint32_t)d.n * (uint32_t)width * 512u;
+            const uint32_t wbytes = (uint32_t)d.n * (uint32_t)width * (uint32_t)geo.CB;
             const int g_first = grp(d.kb), ng = grp(d.kb + d.n - 1) - g_first + 1;
             if (pl == 0) {
                 mbar_arrive_expect_tx(&full[slot], wbytes);
@@ -364,6 +404,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
             const int p_chunks = d.n * NT * kTileBytes / 16;
             const int8_t* psrc = p.pieces + (size_t)d.kb * NT * kTileBytes;
             for (int i = pl; i < p_chunks; i += 32 * kProducerWarps) cp_async16(st + L::kX + 16 * i, psrc + 16 * i);
+            if constexpr (WB == 2)
+                for (int i = pl; i < d.n * 4; i += 32 * kProducerWarps)
+                    cp_async16(st + L::kXK + 16 * i, p.xkb + (size_t)d.kb * 16 + 4 * i);
             for (int i = pl; i < ng * 4; i += 32 * kProducerWarps) {
                 cp_async16(st + L::kXS + 16 * i, p.xscale + (size_t)g_first * 16 + 4 * i);
                 if constexpr (L::kBias)
@@ -415,9 +458,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
     OT* C = reinterpret_cast<OT*>(p.C);
     float facc[NT][2];
     int iacc[NT][4];
+    int csum[NT];  // ternary: sum of the fixed-point x over the k-blocks in iacc (per token)
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         facc[j][0] = facc[j][1] = 0.f;
+        csum[j] = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) iacc[j][i] = 0;
     }
@@ -431,11 +476,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
         const float* xs = reinterpret_cast<const float*>(stage + L::kXS + gl * 64);
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
-            const float f = xs[kTokTile * j + t] * 0.0625f;  // 2^-s / 16
-            const int v0 = iacc[j][0] * 256 + iacc[j][1];
-            const int v1 = iacc[j][2] * 256 + iacc[j][3];
+            // int4: the MMA saw 16 q, so 2^-s / 16; ternary: q + 1, so 2^-s and minus sum x
+            const float f = xs[kTokTile * j + t] * (WB == 4 ? 0.0625f : 1.f);
+            const int v0 = iacc[j][0] * 256 + iacc[j][1] - csum[j];
+            const int v1 = iacc[j][2] * 256 + iacc[j][3] - csum[j];
             facc[j][0] = fmaf((float)v0, s0 * f, facc[j][0]);
             facc[j][1] = fmaf((float)v1, s1 * f, facc[j][1]);
+            csum[j] = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) iacc[j][i] = 0;
         }
@@ -545,29 +592,49 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_i8_kernel(const _
         const int b0 = half * kPer + bb;  // this batch: k-blocks [b0, min(b0 + kBatch, n)) of the stage
         const int bn = d.n - b0 < kBatch ? d.n - b0 : kBatch;
         if (sl < width && bn > 0) {
-            const uint32_t unit_bytes = (uint32_t)width * 512u;
-            const uint8_t* wbase = stage + (b0 * (int)unit_bytes) + sl * 512 + lane * 16;
+            constexpr int kCBw = WB == 4 ? 512 : 256, kLaneB = WB == 4 ? 16 : 8;  // chunk and lane bytes
+            const uint32_t unit_bytes = (uint32_t)width * kCBw;
+            const uint8_t* wbase = stage + (b0 * (int)unit_bytes) + sl * kCBw + lane * kLaneB;
             const int g_stage = grp(d.kb);
             const int g_b0 = grp(d.kb + b0);
             int gl = g_b0 - g_stage;                     // scale row of k-block b0
             int gend = (g_b0 + 1) * upg - (d.kb + b0);  // k-blocks of the batch to its group's end
             uint4 wv[kBatch];
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u)
-                wv[u] = u < bn ? *reinterpret_cast<const uint4*>(wbase + u * unit_bytes) : make_uint4(0u, 0u, 0u, 0u);
+            for (int u = 0; u < kBatch; ++u) {
+                if constexpr (WB == 4) {
+                    wv[u] = u < bn ? *reinterpret_cast<const uint4*>(wbase + u * unit_bytes) : make_uint4(0u, 0u, 0u, 0u);
+                } else {
+                    const uint2 v = u < bn ? *reinterpret_cast<const uint2*>(wbase + u * unit_bytes) : make_uint2(0u, 0u);
+                    wv[u] = make_uint4(v.x, v.y, 0u, 0u);
+                }
+            }
             const uint8_t* xbase = stage + L::kX + b0 * L::kXUnit + lane * 16;
 #pragma unroll
             for (int u = 0; u < kBatch; ++u) {
                 if (u >= bn) break;
                 if constexpr (L::kBias)
                     if (p.bias && grp(d.kb + b0 + u) * upg == d.kb + b0 + u) add_bias(stage, gl);
-                const uint32_t l0 = q16_lo(wv[u].x), l1 = q16_lo(wv[u].z), l2 = q16_lo(wv[u].y), l3 = q16_lo(wv[u].w);
-                const uint32_t h0 = q16_hi(wv[u].x), h1 = q16_hi(wv[u].z), h2 = q16_hi(wv[u].y), h3 = q16_hi(wv[u].w);
+                // operands a0..a3 of MMA 0 (l*) and MMA 1 (h*): rows g / g + 8, k-slots 4t.. / 16 + 4t..
+                uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
+                if constexpr (WB == 4) {
+                    l0 = q16_lo(wv[u].x), l1 = q16_lo(wv[u].z), l2 = q16_lo(wv[u].y), l3 = q16_lo(wv[u].w);
+                    h0 = q16_hi(wv[u].x), h1 = q16_hi(wv[u].z), h2 = q16_hi(wv[u].y), h3 = q16_hi(wv[u].w);
+                } else {
+                    t2_operands(wv[u].x, l0, l2, h0, h2);  // column g
+                    t2_operands(wv[u].y, l1, l3, h1, h3);  // column g + 8
+                }
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
                     const uint4 xv = *reinterpret_cast<const uint4*>(xbase + u * L::kXUnit + j * kTileBytes);
-                    imma_16832(iacc[j], l0, l1, l2, l3, xv.x, xv.y);
-                    imma_16832(iacc[j], h0, h1, h2, h3, xv.z, xv.w);
+                    if constexpr (WB == 4) {
+                        imma_16832(iacc[j], l0, l1, l2, l3, xv.x, xv.y);
+                        imma_16832(iacc[j], h0, h1, h2, h3, xv.z, xv.w);
+                    } else {
+                        imma_16832_u8(iacc[j], l0, l1, l2, l3, xv.x, xv.y);
+                        imma_16832_u8(iacc[j], h0, h1, h2, h3, xv.z, xv.w);
+                        csum[j] += *reinterpret_cast<const int*>(stage + L::kXK + (b0 + u) * 64 + 4 * (kTokTile * j + t));
+                    }
                 }
                 if (u + 1 == gend) {
                     flush_ints(stage, gl);
@@ -640,9 +707,9 @@ namespace {
 
 using I8Fn = void (*)(I8Params);
 
-template <int NT, bool RES, typename ST, typename OT>
+template <int NT, bool RES, typename ST, typename OT, int WB = 4>
 std::pair<I8Fn, int> i8_kernel() {
-    return {decode_i8_kernel<NT, RES, ST, OT>, RingI8<NT, ST>::kSmem};
+    return {decode_i8_kernel<NT, RES, WB, ST, OT>, RingI8<NT, WB, ST>::kSmem};
 }
 
 template <typename ST, typename OT>
@@ -662,6 +729,13 @@ std::pair<I8Fn, int> pick_out(DType c, int NT) {
 int i8_tiles(const GemmArgs& a) { return a.a_dtype == DType::F32 ? 2 : (a.M + kTokTile - 1) / kTokTile; }
 
 std::pair<I8Fn, int> select_i8(const GemmArgs& a) {
+    if (a.wbits == 2) {  // ternary: 16-bit activations and scales of the same type, M <= 4
+        if (a.s_dtype == DType::F16)
+            return a.c_dtype == DType::F32 ? i8_kernel<1, false, __half, float, 2>()
+                                           : i8_kernel<1, false, __half, __half, 2>();
+        return a.c_dtype == DType::F32 ? i8_kernel<1, false, __nv_bfloat16, float, 2>()
+                                       : i8_kernel<1, false, __nv_bfloat16, __nv_bfloat16, 2>();
+    }
     if (a.a_dtype == DType::F32) {
         // fp32 activations: fp32 output (hq_gemm's rule c_dtype == a_dtype or f32)
         if (a.s_dtype == DType::F16) return i8_kernel<2, true, __half, float>();
@@ -696,6 +770,11 @@ size_t xscale_bytes(int K) { return ((size_t)(K / kBlockK) * 64 + 255) & ~(size_
 }  // namespace
 
 bool decode_i8_supported(const GemmArgs& a) {
+    if (a.wbits == 2) {  // ternary: one tile of 4 token slots, 16-bit activations, scales of their type
+        if (a.M < 1 || a.M > 4 || a.bias || (a.a_dtype != DType::F16 && a.a_dtype != DType::BF16)) return false;
+        if (a.s_dtype != a.a_dtype || (a.c_dtype != a.a_dtype && a.c_dtype != DType::F32)) return false;
+        return a.group % kBlockK == 0 && a.K % a.group == 0;
+    }
     if (a.wbits != 4 || a.M < 1 || a.M > 8) return false;  // one or two tiles of 4 token slots
     if (a.a_dtype == DType::F32) {
         if (a.M > 4 || a.c_dtype != DType::F32) return false;
@@ -709,9 +788,9 @@ bool decode_i8_supported(const GemmArgs& a) {
     return a.group % kBlockK == 0 && a.K % a.group == 0;
 }
 
-// split state, activation pieces, x scales, x sums
+// split state, activation pieces, x scales, x sums per scale group, x sums per k-block (ternary)
 size_t decode_i8_workspace_bytes(int N, int K, int dev) {
-    return split_bytes(N, K, dev) + pieces_bytes(K) + 2 * xscale_bytes(K);
+    return split_bytes(N, K, dev) + pieces_bytes(K) + 3 * xscale_bytes(K);
 }
 
 cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
@@ -724,6 +803,8 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     int8_t* pieces = reinterpret_cast<int8_t*>(a.ws + split);
     float* xscale = reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K));
     float* xsum = a.bias ? reinterpret_cast<float*>(a.ws + split + pieces_bytes(a.K) + xscale_bytes(a.K)) : nullptr;
+    int* xkb = a.wbits == 2 ? reinterpret_cast<int*>(a.ws + split + pieces_bytes(a.K) + 2 * xscale_bytes(a.K))
+                            : nullptr;
 
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -738,13 +819,13 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     pc.numAttrs = 1;
     if (a.a_dtype == DType::F16)
         e = cudaLaunchKernelEx(&pc, x_prep_kernel<__half, false>, static_cast<const __half*>(a.A), a.M, a.K, a.group,
-                               NT * kTokTile, pieces, xscale, xsum);
+                               NT * kTokTile, pieces, xscale, xsum, xkb);
     else if (a.a_dtype == DType::BF16)
         e = cudaLaunchKernelEx(&pc, x_prep_kernel<__nv_bfloat16, false>, static_cast<const __nv_bfloat16*>(a.A), a.M,
-                               a.K, a.group, NT * kTokTile, pieces, xscale, xsum);
+                               a.K, a.group, NT * kTokTile, pieces, xscale, xsum, xkb);
     else
         e = cudaLaunchKernelEx(&pc, x_prep_kernel<float, true>, static_cast<const float*>(a.A), a.M, a.K, a.group,
-                               NT * kTokTile, pieces, xscale, xsum);
+                               NT * kTokTile, pieces, xscale, xsum, static_cast<int*>(nullptr));
     if (e != cudaSuccess) return e;
 
     // 2. the GEMM
@@ -759,6 +840,7 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     p.pieces = pieces;
     p.xscale = xscale;
     p.xsum = xsum;
+    p.xkb = xkb;
     p.C = a.C;
     p.err = device_error_word(dev);
     p.counters = reinterpret_cast<unsigned*>(a.ws);

@@ -142,6 +142,24 @@ def test_decode_ternary_parity(K, N, M, dtype):
     assert o.max_rel_err(y, ref) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("K,N,g", [(512, 16384, 128), (1024, 16400, 64), (2048, 16640, 256), (5120, 34816, 128)])
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_decode_ternary_integer_path(K, N, g, M, dtype):
+    """Ternary weights on the integer-MMA stream kernel (layers of >= 128 strip groups, M <= 4):
+    codes q + 1 as u8 MMA operands, the "- 1" restored from per-k-block sums of the fixed-point
+    activations.  Ragged width (16400 = 1025 strips), groups 64 / 128 / 256, 16-bit and fp32 outputs."""
+    A, t, S = o.gen_ternary_case(M, K, N, group=g, seed=K + N + M, a_dtype=dtype)
+    ref = o.t2_gemm(A, o.pack_linear_t2(t), S, group=g)
+    W = cuda(o.pack_tile(t, 2), None)
+    y = run_gemm(A, W, S.astype(np.float32), N, g, dtype, wfmt=_lib.HQ_WFMT_TILE_T2, s_dtype=dtype)
+    assert o.max_rel_err(y, ref) <= TOL[dtype]
+    if dtype == "f16":  # scales exact in fp16 (the generator rounds them so): fp32 output to 1e-4
+        y32 = run_gemm(A, W, S.astype(np.float32), N, g, dtype, wfmt=_lib.HQ_WFMT_TILE_T2, s_dtype=dtype,
+                       out_dtype=torch.float32)
+        assert o.max_rel_err(y32, ref) <= 1e-4
+
+
 @pytest.mark.parametrize("M", [1, 4, 8])
 def test_f32_activations_with_bias_match_reference_semantics(M):
     """The reference's own form: fp32 X, fp32 scale and bias, w = u*s + b (marlin_gemm.cu:208-209),

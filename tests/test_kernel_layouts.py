@@ -241,3 +241,48 @@ def test_int8_decode_fragments_give_16q_dot_x(seed):
     want = 16 * (q.astype(np.int64).T @ xf.T)  # [n][m]
     for m in range(M):
         assert np.array_equal(256 * D[:, 2 * m] + D[:, 2 * m + 1], want[:, m])
+
+
+def _prmt(a, b, sel):
+    """PTX prmt.b32 (default mode): byte i of the result is byte (sel >> 4i) & 7 of a (bytes 0-3)
+    followed by b (bytes 4-7)."""
+    src = list(int(a).to_bytes(4, "little")) + list(int(b).to_bytes(4, "little"))
+    return sum(src[(sel >> (4 * i)) & 7] << (8 * i) for i in range(4))
+
+
+def _t2_operands(w):
+    """hq_decode_i8.cu t2_operands: one TILE_T2 word -> (MMA 0 slots 4t.., MMA 0 slots 16+4t.., MMA 1 ...)."""
+    f0, f1 = w & 0x03030303, (w >> 2) & 0x03030303
+    f2, f3 = (w >> 4) & 0x03030303, (w >> 6) & 0x03030303
+    return _prmt(f0, f1, 0x6240), _prmt(f0, f1, 0x7351), _prmt(f2, f3, 0x6240), _prmt(f2, f3, 0x7351)
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_int8_decode_ternary_fragments_give_q_dot_x(seed):
+    """The integer decode kernel's ternary operands: codes c = q + 1 as u8 in the int4 path's k-slot
+    order, so that with the same activation pieces sum c x - sum x = sum q x (one 64-k block)."""
+    rng = np.random.default_rng(100 + seed)
+    K, N, M = 64, 16, 4
+    t = rng.integers(-1, 2, size=(K, N), dtype=np.int8)
+    tile = o.pack_tile(t, 2).view(np.uint32)  # one chunk: 16 columns x 64 k, 2 words per lane
+    xf = rng.integers(-16384, 16385, size=(M, K))
+    h = (xf + 128) >> 8
+    l = xf - 256 * h
+    pieces = np.zeros((M * 2 * 4, 16), np.int8)
+    for m in range(M):
+        for p, arr in enumerate((h, l)):
+            for tt in range(4):
+                pieces[(m * 2 + p) * 4 + tt] = [arr[m, 16 * tt + _PIECE_POS[j]] for j in range(16)]
+    xbytes = pieces.reshape(-1).view(np.uint32).reshape(32, 4)
+    a0, a1 = [], []
+    for lane in range(32):
+        x, y = int(tile[2 * lane]), int(tile[2 * lane + 1])  # columns g and g + 8
+        l0, l2, h0, h2 = _t2_operands(x)
+        l1, l3, h1, h3 = _t2_operands(y)
+        a0.append([l0, l1, l2, l3])
+        a1.append([h0, h1, h2, h3])
+    D = _mma_m16n8k32(a0, [xbytes[lane][0:2] for lane in range(32)]) + \
+        _mma_m16n8k32(a1, [xbytes[lane][2:4] for lane in range(32)])
+    want = t.astype(np.int64).T @ xf.T  # [n][m]
+    for m in range(M):
+        assert np.array_equal(256 * D[:, 2 * m] + D[:, 2 * m + 1] - xf[m].sum(), want[:, m])
