@@ -32,7 +32,8 @@ def run(A, W, S, N, g, dtype, wfmt=_lib.HQ_WFMT_TILE_U4, out_dtype=None):
 
 
 @pytest.mark.parametrize("M,K,N,g", [(17, 64, 16, 64), (64, 256, 48, 128), (128, 512, 256, 128),
-                                     (130, 384, 272, 128), (300, 1024, 1040, 128), (257, 640, 896, 128)])
+                                     (130, 384, 272, 128), (300, 1024, 1040, 128), (257, 640, 896, 128),
+                                     (200, 512, 272, 64), (200, 1024, 400, 256), (40, 192, 32, 64)])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_prefill_int4_small(M, K, N, g, dtype):
     A, q, S = o.gen_int4_case(M, K, N, group=g, seed=M + K + N, a_dtype=dtype)
