@@ -574,34 +574,33 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
     g.manual_seed(4242 + rank)
     X = {name: torch.randn((rows, specs[name].K), device=dev, generator=g).bfloat16() for name, _, _ in tp.LAYER_SHAPES}
     Y = {name: torch.empty((rows, specs[name].N), device=dev, dtype=torch.bfloat16) for name, _, _ in tp.LAYER_SHAPES}
-    # Micro-batches (rows split on 256-row tile boundaries), each on its own stream with its own
-    # workspace and all-reduce flags: one micro-batch's all-reduce runs while the other's GEMM
-    # does (the all-reduce kernel fits on the SMs beside the persistent GEMM).  Within a
-    # micro-batch every GEMM and all-reduce is in order.
+    # Micro-batches (rows split on 256-row tile boundaries): their GEMMs run in order on the
+    # compute stream, their all-reduces in the same order on one communication stream, so one
+    # micro-batch's all-reduce overlaps the next GEMM (of the other micro-batch), and each
+    # micro-batch's next GEMM waits for its own all-reduce, as the next layer's input would.
+    # One collective at a time per GPU: a spinning collective never waits for a peer whose
+    # matching kernel is kept off its SMs by another spinning one.
     n_mb = max(1, min(args.stack_mb, rows // 256)) if world > 1 else 1
     tiles = rows // 256
-    bounds = [rows * 0] + [256 * ((tiles * (i + 1) + n_mb - 1) // n_mb) for i in range(n_mb)]
+    bounds = [0] + [256 * ((tiles * (i + 1) + n_mb - 1) // n_mb) for i in range(n_mb)]
     bounds[-1] = rows
     mbs = [(bounds[i], bounds[i + 1]) for i in range(n_mb)]
-    streams = [stream] + [torch.cuda.Stream(device=dev) for _ in range(n_mb - 1)]
+    comm = torch.cuda.Stream(device=dev) if world > 1 else stream
     ws_bytes = max(int(L.hq_gemm_workspace_size(rows, specs[n].N, specs[n].K, GROUP, _lib.HQ_WFMT_TILE_U4))
                    for n, _, _ in tp.LAYER_SHAPES)
-    wss = [torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=dev) for _ in range(n_mb)]
+    ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
 
     # The all-reduce after O and down: hq_allreduce_sum over NVLink peer memory
     # (the row-parallel outputs live in PyTorch symmetric memory), or NCCL.
     use_hq = world > 1 and args.stack_comm == "hq"
-    epoch = [0] * n_mb
+    epoch = [0]
     if use_hq:
         import ctypes
         import torch.distributed._symmetric_memory as symm
-        fptrs, flag_bufs = [], []
-        for _ in range(n_mb):
-            flags = symm.empty(32, dtype=torch.int32, device=dev)
-            flags.zero_()
-            hf = symm.rendezvous(flags, dist.group.WORLD)
-            flag_bufs.append((flags, hf))
-            fptrs.append((ctypes.c_void_p * world)(*hf.buffer_ptrs))
+        flags = symm.empty(32, dtype=torch.int32, device=dev)
+        flags.zero_()
+        hf = symm.rendezvous(flags, dist.group.WORLD)
+        fptrs = (ctypes.c_void_p * world)(*hf.buffer_ptrs)
         peers = {}
         for name in tp.ROW_PARALLEL:
             buf = symm.empty((rows, specs[name].N), dtype=torch.bfloat16, device=dev)
@@ -612,42 +611,44 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
         torch.cuda.synchronize()
         dist.barrier()
 
-    def all_reduce(name, mb):
+    def all_reduce(name, mb):  # on the communication stream
         r0, r1 = mbs[mb]
         n_el = (r1 - r0) * specs[name].N
         if use_hq:
-            epoch[mb] += 1
+            epoch[0] += 1
             off = r0 * specs[name].N * 2
             ptrs, _, mc = peers[name]
             bp = (ctypes.c_void_p * world)(*[q + off for q in ptrs])
-            st = L.hq_allreduce_sum(bp, fptrs[mb], ctypes.c_void_p(mc + off if mc else 0), world, rank,
-                                    _lib.HQ_BF16, n_el, epoch[mb], args.ar_ctas,
-                                    ctypes.c_void_p(streams[mb].cuda_stream))
+            st = L.hq_allreduce_sum(bp, fptrs, ctypes.c_void_p(mc + off if mc else 0), world, rank,
+                                    _lib.HQ_BF16, n_el, epoch[0], args.ar_ctas, ctypes.c_void_p(comm.cuda_stream))
             if st != 0:
                 raise RuntimeError(L.hq_last_error_string().decode())
         else:
-            with torch.cuda.stream(streams[mb]):
+            with torch.cuda.stream(comm):
                 dist.all_reduce(Y[name][r0:r1])
 
     def step():
-        if n_mb > 1:  # the micro-batch streams start after everything queued on `stream`
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            for sm in streams[1:]:
-                sm.wait_event(ev)
+        pending = [None] * n_mb  # each micro-batch's last all-reduce, not yet waited for
         for layer in range(layers):
             for name, _, _ in tp.LAYER_SHAPES:
                 sp = specs[name]
                 Wt, St = W[layer][name]
                 for mb, (r0, r1) in enumerate(mbs):
+                    if pending[mb] is not None:
+                        stream.wait_event(pending[mb])
+                        pending[mb] = None
                     _gemm_call(L, _lib, X[name][r0:r1], _lib.HQ_BF16, Wt, _lib.HQ_WFMT_TILE_U4, St, _lib.HQ_BF16,
-                               Y[name][r0:r1], _lib.HQ_BF16, r1 - r0, sp.N, sp.K, wss[mb], streams[mb])
+                               Y[name][r0:r1], _lib.HQ_BF16, r1 - r0, sp.N, sp.K, ws, stream)
                     if sp.row_parallel and world > 1:
+                        done = torch.cuda.Event()
+                        done.record(stream)
+                        comm.wait_event(done)
                         all_reduce(name, mb)
-        for sm in streams[1:]:  # and `stream` waits for them at the end of the step
-            ev = torch.cuda.Event()
-            ev.record(sm)
-            stream.wait_event(ev)
+                        pending[mb] = torch.cuda.Event()
+                        pending[mb].record(comm)
+        for ev in pending:  # the step ends when its last all-reduces have
+            if ev is not None:
+                stream.wait_event(ev)
 
     with torch.cuda.stream(stream):
         for _ in range(2):
@@ -680,7 +681,7 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
             torch.cuda.synchronize()
             dist.barrier()
             peers.clear()
-    del W, X, Y, wss
+    del W, X, Y, ws
     torch.cuda.empty_cache()
     return {"metric": "TP layer-stack TFLOP/s (BASELINE configs[4])", "value": tf, "unit": "TFLOP/s",
             "tokens_per_s": rows / (ms / 1e3), "ms_per_step": ms, "n_gpus": world, "layers": layers,
@@ -689,7 +690,7 @@ def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
             "collective": collective, "micro_batches": [r1 - r0 for r0, r1 in mbs],
             "timing": f"{steps} steps after 2 warm-up, CUDA events on the compute stream, max over ranks; "
                       "64 x 4 hq_gemm launches + 128 all-reduces per step and micro-batch at TP; the "
-                      "micro-batches run on their own streams, so one's all-reduce overlaps the other's GEMM"}
+                      "all-reduces run on a communication stream, overlapping the other micro-batch's GEMM"}
 
 
 def run_case(args):
@@ -772,8 +773,9 @@ def main():
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")
-    ap.add_argument("--stack-mb", type=int, default=2,
-                    help="micro-batches of the TP stack at N > 1 (each step's rows split on 256-row tiles)")
+    ap.add_argument("--stack-mb", type=int, default=1,
+                    help="micro-batches of the TP stack at N > 1 (each step's rows split on 256-row tiles; two "
+                         "measured slower at 2 GPUs: 1500 against 1760 TFLOP/s)")
     ap.add_argument("--ar-ctas", type=int, default=128, help="CTAs of hq_allreduce_sum in the TP stack")
     ap.add_argument("--sweep-comm", default="nccl", choices=["hq", "nccl"],
                     help="all-reduce of the row-parallel outputs in the tensor-parallel decode sweep (10-160 KB "
