@@ -1,9 +1,12 @@
 // hq_decode_i8.cu -- decode GEMM (M <= 8) on the integer tensor cores:
-// int4 codes x fp16/bf16 activations through mma.sync s8 x s8 -> s32.
+// int4 (or ternary) codes x fixed-point activations through mma.sync
+// s8 x s8 -> s32 (u8 x s8 for ternary).
 //
-// Replaces, for int4 weights, 16-bit activations and no bias, the reference's
-// kernel_marlin_gemm_int4_templated / _dynamic and its memset + atomicAdd
-// split-K (hydrogen/src/model/marlin_gemm.cu:130-322, :556-601).
+// Replaces the reference's kernel_marlin_gemm_int4_templated / _dynamic and
+// its memset + atomicAdd split-K (hydrogen/src/model/marlin_gemm.cu:130-322,
+// :556-601) for the calls the dispatcher (hq_decode.cu) sends here: fp16 /
+// bf16 activations, fp32 activations (two fixed-point parts), fp32 scales with
+// the reference's bias, and this library's 2-bit ternary tiles.
 //
 // Why integers: a decode GEMM reads every weight byte once, so its speed is set
 // by how few instructions turn a byte of codes into tensor-core operands.
