@@ -547,6 +547,69 @@ def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
             "per_gemm": rows}
 
 
+def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
+    """GGUF Q4_K at model load: hq_q4_k_to_tile_u4 (GB/s of Q4_K blocks in) and the group-32 GEMM it
+    feeds (fp16 activations, f32 scale and bias rows per 32 weights) at the 27B shapes, M in {1, 16}.
+    Decode GB/s counts the bytes the kernel must read: codes (K N / 2) plus 8 bytes of scale and bias
+    per 32 weights, activations and outputs."""
+    import ctypes
+    vp = ctypes.c_void_p
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    half_bits = torch.tensor([0.002], dtype=torch.float16).view(torch.uint8).to(dev)  # d = dmin = 0.002
+    rows, conv = [], []
+    dec_bytes, dec_ms = 0.0, 0.0
+    for name, K, N in SHAPES:
+        nblk = N * (K // 256)
+        copies = []
+        for c in range(args.copies):
+            blob = torch.randint(0, 256, (nblk, 144), dtype=torch.uint8, device=dev, generator=g)
+            blob[:, 0:2] = half_bits
+            blob[:, 2:4] = half_bits
+            tile = torch.empty(hq.weight_bytes(_lib.HQ_WFMT_TILE_U4, K, N), dtype=torch.uint8, device=dev)
+            S = torch.empty((K // 32, N), device=dev)
+            B = torch.empty((K // 32, N), device=dev)
+            copies.append((blob, tile, S, B))
+
+        def cv(c):
+            blob, tile, S, B = copies[c]
+            st = L.hq_q4_k_to_tile_u4(vp(blob.data_ptr()), vp(tile.data_ptr()), vp(S.data_ptr()), vp(B.data_ptr()),
+                                      K, N, vp(stream.cuda_stream))
+            if st != 0:
+                raise RuntimeError(L.hq_last_error_string().decode())
+        ms = _time_launches(torch, stream, cv, len(copies), reps=10)
+        conv.append({"shape": name, "K": K, "N": N, "us": round(ms * 1e3, 1),
+                     "GBps_in": round(nblk * 144 / (ms / 1e3) / 1e9, 1)})
+        copies = [(t, s, b) for (_, t, s, b) in copies]
+        for M in (1, 16):
+            A = torch.randn((M, K), device=dev, generator=g).half()
+            C = torch.empty((M, N), device=dev, dtype=torch.float16)
+            nb = int(L.hq_gemm_workspace_size(M, N, K, 32, _lib.HQ_WFMT_TILE_U4))
+            ws = torch.zeros(max(nb, 16), dtype=torch.uint8, device=dev)
+
+            def fn(c):
+                t, s, b = copies[c]
+                st = L.hq_gemm(vp(A.data_ptr()), _lib.HQ_F16, vp(t.data_ptr()), _lib.HQ_WFMT_TILE_U4, vp(s.data_ptr()),
+                               _lib.HQ_F32, vp(b.data_ptr()), vp(C.data_ptr()), _lib.HQ_F16, M, N, K, 32,
+                               vp(ws.data_ptr()), ws.numel(), vp(stream.cuda_stream))
+                if st != 0:
+                    raise RuntimeError(L.hq_last_error_string().decode())
+            ms = _time_launches(torch, stream, fn, len(copies), reps=20)
+            nbytes = K * N // 2 + 2 * (K // 32) * N * 4 + M * K * 2 + M * N * 2
+            dec_bytes += nbytes
+            dec_ms += ms
+            rows.append({"shape": name, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
+                         "GBps": round(nbytes / (ms / 1e3) / 1e9, 1)})
+            del A, C, ws
+        del copies
+    dec = dec_bytes / (dec_ms / 1e3) / 1e9
+    return {"metric": "GGUF Q4_K: load-time conversion and group-32 decode GEMM",
+            "decode_GBps": dec, "decode_frac_hbm": dec / peaks["hbm_gbs"], "dtype": "f16",
+            "timing": "per call: CUDA events around 20 GEMMs / 10 conversions queued behind a spin kernel, after "
+                      "3 warm-up, rotating weight copies (not graph-captured)",
+            "conversion": conv, "per_gemm": rows}
+
+
 # ------------------------------------------------- TP layer stack (configs[4])
 
 def tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args):
@@ -1024,13 +1087,14 @@ def main():
         stack = tp_stack(torch, dist, L, _lib, dev, world, rank, stream, peaks, args)
         hq.check_device_error()
 
-    prefill = ternary = tq1 = proj = w8 = None
+    prefill = ternary = tq1 = proj = w8 = q4k = None
     if world == 1 and not args.no_extra:
         prefill = prefill_sweep(torch, L, _lib, hq, dev, stream, weights, peaks, args)
         ternary = ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
         tq1 = tq1_sweep(torch, L, _lib, dev, stream, peaks, args)
         proj = proj_sweep(torch, L, _lib, dev, stream, peaks, args)
         w8 = w8_sweep(torch, L, _lib, dev, stream, peaks, args)
+        q4k = q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args)
         hq.check_device_error()
 
     cpu = None
@@ -1097,6 +1161,8 @@ def main():
             line["output_projection"] = proj
         if w8 is not None:
             line["w8a8"] = w8
+        if q4k is not None:
+            line["q4_k"] = q4k
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

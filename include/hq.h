@@ -22,9 +22,15 @@
  *   - Calls are asynchronous on `stream`, stream-ordered, allocate nothing,
  *     and may run concurrently on different streams with different
  *     workspaces.  C is overwritten.
- *   - Shapes: N % 16 == 0, K % 64 == 0, group % 64 == 0, K % group == 0
- *     (the reference needs K % 512 == 0 and group % 32 == 0: marlin_gemm.cu
- *     :156-159, so every reference shape with group >= 64 is accepted).
+ *   - Shapes: N % 16 == 0, K % 64 == 0, group == 32 or group % 64 == 0,
+ *     K % group == 0 (the reference needs K % 512 == 0 and group % 32 == 0:
+ *     marlin_gemm.cu:156-159, so every reference shape with group 32 or a
+ *     multiple of 64 is accepted).  Group 32 takes int4 weights with f32
+ *     scales and runs on the split-K decode kernel for every M (16 rows per
+ *     launch): each 64-k block carries two scale (and bias) rows and every
+ *     MMA step runs once per 32-k half.  27B shapes at M = 1 with a bias
+ *     (the Q4_K form) take 1.2-2.1x the time of a group-128 fp16 layer, for
+ *     1.47x the bytes.
  */
 #ifndef HQ_H
 #define HQ_H
@@ -213,6 +219,23 @@ HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out,
  */
 HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* scales_f16,
                                      int K, int N, hq_stream_t stream);
+
+/*
+ * Model-load conversion of GGUF Q4_K weights (type 12: 256 weights per 144-byte
+ * block, gguf_parser.hpp:44,130; laid out [N][K/256] as the native decoder maps
+ * GGUF tensors, native_decoder.cu:849-918) into TILE_U4 codes plus f32 group-32
+ * scales and biases [K/32][N].  The block fields follow llama.cpp's block_q4_K:
+ * fp16 d and dmin, 6-bit scale sc_i and min m_i per 32 weights, 4-bit codes u.
+ * Then hq_gemm(A, a, tile_u4, HQ_WFMT_TILE_U4, scales, HQ_F32, bias, C, c, M, N,
+ * K, 32, ...) computes with w = u * (d sc_i) - dmin m_i, llama.cpp's
+ * dequantize_row_q4_K; scale and bias are exact in f32.
+ * K % 256 == 0, N % 16 == 0; w_q4k 8-byte aligned, the outputs 4-byte aligned.
+ * The _host form runs on host threads (nthreads <= 0: all) with host pointers.
+ */
+HQ_API hq_status hq_q4_k_to_tile_u4(const void* w_q4k, void* tile_u4, float* scales, float* bias,
+                                    int K, int N, hq_stream_t stream);
+HQ_API hq_status hq_q4_k_to_tile_u4_host(const void* w_q4k, void* tile_u4, float* scales, float* bias,
+                                         int K, int N, int nthreads);
 
 /*
  * W8A8 GEMM, the reference engine's third precision: activations quantized per

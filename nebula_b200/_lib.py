@@ -36,6 +36,8 @@ SIGNATURES = {
     "hq_repack_device": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "hq_tq1_0_gemv": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "hq_tq1_0_to_tile_t2": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "hq_q4_k_to_tile_u4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "hq_q4_k_to_tile_u4_host": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "hq_w8_gemm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "hq_output_projection": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
     "hq_embedding_lookup": (_i, [_vp, _i, _i, _vp, _i, _i, _vp]),

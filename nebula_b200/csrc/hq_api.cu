@@ -162,8 +162,8 @@ hq_status check_shape(int M, int N, int K, int group) {
     if (M < 0 || N <= 0 || K <= 0) return fail(HQ_ERR_INVALID_ARG, "negative or zero size M=%d N=%d K=%d", M, N, K);
     if (N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "N=%d must be a multiple of 16", N);
     if (K % 64) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "K=%d must be a multiple of 64", K);
-    if (group <= 0 || group % 64 || K % group)
-        return fail(HQ_ERR_UNSUPPORTED_SHAPE, "group=%d must be a multiple of 64 dividing K=%d", group, K);
+    if (group <= 0 || (group % 64 && group != 32) || K % group)
+        return fail(HQ_ERR_UNSUPPORTED_SHAPE, "group=%d must be 32 or a multiple of 64 dividing K=%d", group, K);
     return HQ_OK;
 }
 
@@ -367,6 +367,29 @@ HQ_API hq_status hq_repack_device(const void* src, hq_wfmt src_fmt, void* dst, h
             return fail(HQ_ERR_INVALID_ARG, "unsupported repack %d -> %d", (int)src_fmt, (int)dst_fmt);
     }
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "repack launch");
+}
+
+HQ_API hq_status hq_q4_k_to_tile_u4(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
+                                    hq_stream_t stream) {
+    if (!w_q4k || !tile_u4 || !scales || !bias) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (K <= 0 || N <= 0 || K % 256 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "need K %% 256 == 0, N %% 16 == 0");
+    if (((uintptr_t)w_q4k & 7u) || ((uintptr_t)tile_u4 & 3u) || ((uintptr_t)scales & 3u) || ((uintptr_t)bias & 3u))
+        return fail(HQ_ERR_MISALIGNED, "w_q4k must be 8-byte aligned, tile_u4 / scales / bias 4-byte aligned");
+    int dev = 0;
+    hq_status st = check_device(&dev);
+    if (st != HQ_OK) return st;
+    cudaError_t e = launch_q4k_to_tile(static_cast<const uint8_t*>(w_q4k), static_cast<uint8_t*>(tile_u4), scales,
+                                       bias, K, N, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HQ_OK : cuda_fail(e, "Q4_K conversion launch");
+}
+
+HQ_API hq_status hq_q4_k_to_tile_u4_host(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
+                                         int nthreads) {
+    if (!w_q4k || !tile_u4 || !scales || !bias) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
+    if (K <= 0 || N <= 0 || K % 256 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "need K %% 256 == 0, N %% 16 == 0");
+    host::q4k_to_tile(static_cast<const uint8_t*>(w_q4k), static_cast<uint32_t*>(tile_u4), scales, bias, K, N,
+                      nthreads);
+    return HQ_OK;
 }
 
 HQ_API hq_status hq_tq1_0_gemv(const float* x, const void* w, float* out, int in_dim, int out_dim,

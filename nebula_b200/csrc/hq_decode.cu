@@ -48,8 +48,9 @@ constexpr int kMaxRows = 16;
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-// Shared-memory layout of one pipeline stage.
-template <int WBITS, typename AT, typename ST, bool kBias>
+// Shared-memory layout of one pipeline stage.  kG32: scale groups of 32 k, so
+// each 64-k block has two scale (and bias) rows.
+template <int WBITS, typename AT, typename ST, bool kBias, bool kG32>
 struct Stage {
     static constexpr int kCB = WBITS == 4 ? 512 : 256;
     static constexpr int kWBytes = kUPS * kGroupStrips * kCB;  // weights of a full group
@@ -59,8 +60,11 @@ struct Stage {
     static constexpr int kXRow = kXTma ? 128 : kXRowBytes + 16;   // 128B-swizzled rows / padded rows
     static constexpr int kXUnit = kMaxRows * kXRow;
     static constexpr int kSElt = (int)sizeof(ST);
-    static constexpr int kSUnit = kGroupCols * kSElt;
-    static constexpr int kBUnit = kBias ? kGroupCols * 4 : 0;
+    static constexpr int kSRows = kG32 ? 2 : 1;  // scale rows per k-block
+    static constexpr int kSRow = kGroupCols * kSElt;
+    static constexpr int kSUnit = kSRows * kSRow;
+    static constexpr int kBRow = kGroupCols * 4;
+    static constexpr int kBUnit = kBias ? kSRows * kBRow : 0;
     static constexpr int kX = align_up(kWBytes, 1024);  // swizzled TMA destination: 1024-byte aligned
     static constexpr int kS = kX + kUPS * kXUnit;
     static constexpr int kB = kS + kUPS * kSUnit;
@@ -201,9 +205,9 @@ __device__ __forceinline__ float lds_scale(const uint8_t* sp) {
     return to_f32(*reinterpret_cast<const ST*>(sp));
 }
 
-template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
+template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32>
 __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using L = Stage<WBITS, AT, ST, kBias>;
+    using L = Stage<WBITS, AT, ST, kBias, kG32>;
     constexpr bool kSplit = std::is_same<AT, float>::value;
     constexpr bool kBF16 = ComputeType<AT>::bf16;  // float activations compute in fp16
     constexpr int kCB = L::kCB;
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
     const int n_iters = (n_units + kUPS - 1) / kUPS;
     const uint32_t unit_bytes = (uint32_t)width * kCB;  // one k-block of this strip group
     const size_t off0 = geo.unit_offset((long long)sg * KB + kb_begin);
-    const int upg = p.group / kBlockK;  // k-blocks per scale group
+    const int upg = kG32 ? 1 : p.group / kBlockK;  // k-blocks per scale group (group >= 64)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -299,17 +303,23 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
             uint8_t* st = ring + slot * L::kBytes;
             if (lane == 0) {
                 const uint32_t wbytes = (uint32_t)nu * unit_bytes;
-                mbar_arrive_expect_tx(&full[slot], wbytes + (uint32_t)nu * (x_bytes + s_bytes + b_bytes));
+                mbar_arrive_expect_tx(&full[slot],
+                                      wbytes + (uint32_t)nu * (x_bytes + L::kSRows * (s_bytes + b_bytes)));
                 bulk_g2s_hint(st, p.W + off0 + (size_t)it * kUPS * unit_bytes, wbytes, &full[slot], pol);
             }
             __syncwarp();
-            // scale (and bias) row of each k-block: [group][the 128 columns]
+            // scale (and bias) rows of each k-block: [group][the 128 columns]
             if (lane >= 16 && lane < 16 + nu) {
                 const int i = lane - 16;
-                const int gi = (kb_begin + it * kUPS + i) / upg;
-                const size_t off = (size_t)gi * p.N + (size_t)sg * kGroupCols;
-                bulk_g2s(st + L::kS + i * L::kSUnit, Sb + off * L::kSElt, s_bytes, &full[slot]);
-                if constexpr (kBias) bulk_g2s(st + L::kB + i * L::kBUnit, Bb + off * 4, b_bytes, &full[slot]);
+                const int kb = kb_begin + it * kUPS + i;
+#pragma unroll
+                for (int h = 0; h < L::kSRows; ++h) {
+                    const int gi = kG32 ? 2 * kb + h : kb / upg;
+                    const size_t off = (size_t)gi * p.N + (size_t)sg * kGroupCols;
+                    bulk_g2s(st + L::kS + i * L::kSUnit + h * L::kSRow, Sb + off * L::kSElt, s_bytes, &full[slot]);
+                    if constexpr (kBias)
+                        bulk_g2s(st + L::kB + i * L::kBUnit + h * L::kBRow, Bb + off * 4, b_bytes, &full[slot]);
+                }
             }
             if (it >= early) {
                 issue_x(it);
@@ -335,6 +345,14 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
         const int g = lane >> 2, t = lane & 3;
         using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
         const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
+        // Group-32 scales: lane t's activation fragments hold k [16t, 16t + 16)
+        // of a block (tile order), so lanes t < 2 carry scale group 2kb and
+        // lanes t >= 2 group 2kb + 1.  Each MMA runs once per group with the
+        // other group's lanes zeroed, keeping the two sums apart.
+        auto half_mask = [&](int h) -> uint32_t {
+            if constexpr (kG32) return ((t >> 1) == h) ? 0xffffffffu : 0u;
+            else return 0xffffffffu;
+        };
         // After a timed-out wait the warp stops waiting but keeps the same
         // control flow (results are garbage, the error word is set): every
         // thread still reaches the barriers below, so nothing hangs.
@@ -351,7 +369,9 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
             // Activation fragments (and raw-path corrections) of the stage's blocks.
             XF xf[kUPS][MT];
             float corr[kUPS][MT][4];
-            float xs[kUPS][MT][4];
+            // Activation sums for the bias term, per token: the ones-MMA gives rows
+            // g and g + 8 the same value, so only its c0 / c1 are kept.
+            float xs[kUPS][L::kSRows][MT][2];
 #pragma unroll
             for (int u = 0; u < kUPS; ++u) {
                 if (u >= nu) continue;
@@ -385,17 +405,22 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                 if constexpr (kBias) {
                     const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
 #pragma unroll
-                    for (int m = 0; m < MT; ++m) {
+                    for (int h = 0; h < L::kSRows; ++h) {
+                        const uint32_t mk = half_mask(h);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) xs[u][m][i] = 0.f;
+                        for (int m = 0; m < MT; ++m) {
+                            float x4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int s = 0; s < 4; ++s) {
-                            if constexpr (kSplit) {
-                                mma_16816<false>(xs[u][m], ones, xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
-                                mma_16816<false>(xs[u][m], ones, xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
-                            } else {
-                                mma_16816<kBF16>(xs[u][m], ones, xf[u][m].b0(s), xf[u][m].b1(s));
+                            for (int s = 0; s < 4; ++s) {
+                                if constexpr (kSplit) {
+                                    mma_16816<false>(x4, ones, xf[u][m].hi[2 * s] & mk, xf[u][m].hi[2 * s + 1] & mk);
+                                    mma_16816<false>(x4, ones, xf[u][m].lo[2 * s] & mk, xf[u][m].lo[2 * s + 1] & mk);
+                                } else {
+                                    mma_16816<kBF16>(x4, ones, xf[u][m].b0(s) & mk, xf[u][m].b1(s) & mk);
+                                }
                             }
+                            xs[u][h][m][0] = x4[0];
+                            xs[u][h][m][1] = x4[1];
                         }
                     }
                 }
@@ -406,6 +431,60 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                 const int sl = kStripsPerWarp * warp + j;
                 if (sl >= width) continue;
                 const int nl = sl * kStripCols + g;
+                if constexpr (kG32) {
+#pragma unroll
+                    for (int u = 0; u < kUPS; ++u) {
+                        if (u >= nu) continue;
+                        const uint4 wv =
+                            *reinterpret_cast<const uint4*>(stage + u * unit_bytes + sl * kCB + lane * kLaneBytes);
+                        WFrag<WBITS, kBF16, kBias, false> wf;
+                        wf.build(wv);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t mk = half_mask(h);
+                            float tacc[MT][4];
+#pragma unroll
+                            for (int m = 0; m < MT; ++m) {
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) tacc[m][i] = 0.f;
+#pragma unroll
+                                for (int s = 0; s < 4; ++s) {
+                                    if constexpr (kSplit) {
+                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].hi[2 * s] & mk,
+                                                         xf[u][m].hi[2 * s + 1] & mk);
+                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].lo[2 * s] & mk,
+                                                         xf[u][m].lo[2 * s + 1] & mk);
+                                    } else {
+                                        mma_16816<kBF16>(tacc[m], wf.r[s], xf[u][m].b0(s) & mk, xf[u][m].b1(s) & mk);
+                                    }
+                                }
+                            }
+                            const uint8_t* sp = stage + L::kS + u * L::kSUnit + h * L::kSRow;
+                            const float s0 = lds_scale<ST>(sp + nl * L::kSElt);
+                            const float s1 = lds_scale<ST>(sp + (nl + 8) * L::kSElt);
+                            if constexpr (kBias) {
+                                const uint8_t* bp = stage + L::kB + u * L::kBUnit + h * L::kBRow;
+                                const float b0 = lds_scale<float>(bp + nl * 4), b1 = lds_scale<float>(bp + (nl + 8) * 4);
+#pragma unroll
+                                for (int m = 0; m < MT; ++m) {
+                                    acc[j][m][0] += tacc[m][0] * s0 + xs[u][h][m][0] * b0;
+                                    acc[j][m][1] += tacc[m][1] * s0 + xs[u][h][m][1] * b0;
+                                    acc[j][m][2] += tacc[m][2] * s1 + xs[u][h][m][0] * b1;
+                                    acc[j][m][3] += tacc[m][3] * s1 + xs[u][h][m][1] * b1;
+                                }
+                            } else {
+#pragma unroll
+                                for (int m = 0; m < MT; ++m) {
+                                    acc[j][m][0] = fmaf(tacc[m][0], s0, acc[j][m][0]);
+                                    acc[j][m][1] = fmaf(tacc[m][1], s0, acc[j][m][1]);
+                                    acc[j][m][2] = fmaf(tacc[m][2], s1, acc[j][m][2]);
+                                    acc[j][m][3] = fmaf(tacc[m][3], s1, acc[j][m][3]);
+                                }
+                            }
+                        }
+                    }
+                    continue;
+                }
                 float tacc[kUPS][MT][4];  // per-block partial sums (independent MMA chains)
 #pragma unroll
                 for (int u = 0; u < kUPS; ++u) {
@@ -452,10 +531,10 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                         const float b0 = lds_scale<float>(bp + nl * 4), b1 = lds_scale<float>(bp + (nl + 8) * 4);
 #pragma unroll
                         for (int m = 0; m < MT; ++m) {
-                            acc[j][m][0] += tacc[u][m][0] * s0 + xs[u][m][0] * b0;
-                            acc[j][m][1] += tacc[u][m][1] * s0 + xs[u][m][1] * b0;
-                            acc[j][m][2] += tacc[u][m][2] * s1 + xs[u][m][2] * b1;
-                            acc[j][m][3] += tacc[u][m][3] * s1 + xs[u][m][3] * b1;
+                            acc[j][m][0] += tacc[u][m][0] * s0 + xs[u][0][m][0] * b0;
+                            acc[j][m][1] += tacc[u][m][1] * s0 + xs[u][0][m][1] * b0;
+                            acc[j][m][2] += tacc[u][m][2] * s1 + xs[u][0][m][0] * b1;
+                            acc[j][m][3] += tacc[u][m][3] * s1 + xs[u][0][m][1] * b1;
                         }
                     }
                 } else if (same) {
@@ -562,31 +641,45 @@ struct KernelInfo {
     bool x_tma = false;
 };
 
-template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias>
+template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32>
 KernelInfo kernel_info() {
-    using L = Stage<WBITS, AT, ST, kBias>;
-    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias>, L::kSmem, L::kXTma};
+    using L = Stage<WBITS, AT, ST, kBias, kG32>;
+    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias, kG32>, L::kSmem, L::kXTma};
 }
 
 // Output dtype: the activation's own 16-bit type or f32 (f32 activations: f32 out).
-template <int WBITS, int MT, typename AT, typename ST, bool kBias>
+template <int WBITS, int MT, typename AT, typename ST, bool kBias, bool kG32 = false>
 KernelInfo pick_out(DType c) {
-    if (c == DType::F32) return kernel_info<WBITS, MT, AT, ST, float, kBias>();
+    if (c == DType::F32) return kernel_info<WBITS, MT, AT, ST, float, kBias, kG32>();
     if constexpr (std::is_same<AT, __half>::value) {
-        if (c == DType::F16) return kernel_info<WBITS, MT, AT, ST, __half, kBias>();
+        if (c == DType::F16) return kernel_info<WBITS, MT, AT, ST, __half, kBias, kG32>();
     }
     if constexpr (std::is_same<AT, __nv_bfloat16>::value) {
-        if (c == DType::BF16) return kernel_info<WBITS, MT, AT, ST, __nv_bfloat16, kBias>();
+        if (c == DType::BF16) return kernel_info<WBITS, MT, AT, ST, __nv_bfloat16, kBias, kG32>();
     }
     return {};
 }
 
 // Supported (activation, scale, bias) combinations.  int4: (f16,f16), (bf16,bf16),
 // (f16|bf16, f32), (f32, f32) with or without bias for f16/f32 activations, and
-// (f32, f16).  Ternary: (f16,f16), (bf16,bf16).
+// (f32, f16).  Ternary: (f16,f16), (bf16,bf16).  Group 32 (int4, f32 scales):
+// f16 / f32 activations with or without bias, bf16 without.
 template <int WBITS, int MT>
 KernelInfo pick(const GemmArgs& a) {
     const bool bias = a.bias != nullptr;
+    if (a.group % kBlockK) {
+        if constexpr (WBITS == 4) {
+            if (a.group != 32 || a.s_dtype != DType::F32) return {};
+            if (a.a_dtype == DType::F16)
+                return bias ? pick_out<4, MT, __half, float, true, true>(a.c_dtype)
+                            : pick_out<4, MT, __half, float, false, true>(a.c_dtype);
+            if (a.a_dtype == DType::BF16 && !bias) return pick_out<4, MT, __nv_bfloat16, float, false, true>(a.c_dtype);
+            if (a.a_dtype == DType::F32)
+                return bias ? pick_out<4, MT, float, float, true, true>(a.c_dtype)
+                            : pick_out<4, MT, float, float, false, true>(a.c_dtype);
+        }
+        return {};
+    }
     if (a.a_dtype == DType::F16 && a.s_dtype == DType::F16 && !bias)
         return pick_out<WBITS, MT, __half, __half, false>(a.c_dtype);
     if (a.a_dtype == DType::BF16 && a.s_dtype == DType::BF16 && !bias)
@@ -686,7 +779,8 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // against 56.3): this kernel splits them into two fp16 halves and runs
     // twice the MMAs.  Smaller fp32 layers stay here (QKV 17.8 us against 19.4).
     const TileGeom tg(a.K, a.N, a.wbits);
-    const bool i8_shape = a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
+    const bool g64 = a.group % kBlockK == 0;  // group 32 runs only here
+    const bool i8_shape = g64 && a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
                           : a.wbits == 2          ? tg.NSG >= HQ_DECODE_I8_MIN_NSG_T2
                                                   : tg.NSG >= HQ_DECODE_I8_MIN_NSG;
     if (a.M <= HQ_DECODE_I8_MAX_M && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
@@ -694,7 +788,7 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // kernel needs two token tiles there and the tensor-memory kernel's cost does
     // not depend on M (gate_up at M = 16: 34.1 us against 47.1).  Narrower
     // layers stream faster here (QKV at M = 16: 15.2 us against 17.2).
-    if (a.M > 8 && TileGeom(a.K, a.N, a.wbits).NSG >= HQ_DECODE_TC_MIN_NSG && decode_tc_supported(a))
+    if (a.M > 8 && g64 && TileGeom(a.K, a.N, a.wbits).NSG >= HQ_DECODE_TC_MIN_NSG && decode_tc_supported(a))
         return launch_decode_tc(a, false);
     const TileGeom geo(a.K, a.N, a.wbits);
     const KernelInfo ki = select_kernel(a);

@@ -550,7 +550,7 @@ PrefillTsFn ts_pick_out(DType c) {
 
 template <bool PAIR>
 PrefillTsFn ts_select(const GemmArgs& a) {
-    if (a.bias || a.s_dtype != a.a_dtype) return nullptr;
+    if (a.bias || a.s_dtype != a.a_dtype || a.group % BK) return nullptr;
     if (a.a_dtype == DType::F16)
         return a.wbits == 4 ? ts_pick_out<4, __half, PAIR>(a.c_dtype) : ts_pick_out<2, __half, PAIR>(a.c_dtype);
     if (a.a_dtype == DType::BF16)

@@ -7,6 +7,7 @@
 #include "hq_layout.h"
 
 #include <algorithm>
+#include <cstring>
 #include <thread>
 #include <vector>
 
@@ -88,7 +89,123 @@ int grid_for(size_t total) {
     return (int)std::min<size_t>(b, 148 * 16);
 }
 
+// ------------------------------------------------------------------ Q4_K
+// GGUF Q4_K super-block: 256 weights of one row in 144 bytes (the block size
+// hydrogen/include/gguf_parser.hpp:130 gives type 12; the field layout is
+// llama.cpp's published block_q4_K, ggml/src/ggml-common.h):
+//   bytes 0-1   fp16 d, bytes 2-3 fp16 dmin;
+//   bytes 4-15  6-bit scale sc_i and min m_i of each 32-weight sub-block i;
+//   bytes 16-143 codes: quarter j (64 weights) keeps k 64j + l in the low
+//               nibble of byte 32j + l and k 64j + 32 + l in its high nibble.
+// Weight = d * sc_i * u - dmin * m_i   (llama.cpp dequantize_row_q4_K), which
+// is this library's biased form u * scale + bias with group 32, scale =
+// d * sc_i and bias = -(dmin * m_i): both exact in fp32 (11 x 6 bits).
+constexpr int kQ4KBlockBytes = 144;
+
+// IEEE half bits -> float (normals, subnormals, Inf / NaN).
+HQ_HD float half_bits_to_f32(uint32_t h) {
+    const uint32_t sign = (h >> 15) << 31;
+    const int ex = (int)((h >> 10) & 31);
+    uint32_t man = h & 0x3FFu, bits;
+    if (ex == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else if (ex) {
+        bits = sign | ((uint32_t)(ex + 112) << 23) | (man << 13);
+    } else if (!man) {
+        bits = sign;
+    } else {  // subnormal: man * 2^-24, renormalised
+        int e = 113;
+        while (!(man & 0x400u)) {
+            man <<= 1;
+            --e;
+        }
+        bits = sign | ((uint32_t)e << 23) | ((man & 0x3FFu) << 13);
+    }
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(bits);
+#else
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+#endif
+}
+
+// Sub-block i (0..7) of the 12 packed bytes: i < 4 keeps sc / m in the low six
+// bits of bytes i / i + 4; i >= 4 splits them over the low / high nibble of
+// byte i + 4 and the top two bits of bytes i - 4 / i.
+HQ_HD void q4k_scale_min(const uint8_t* p, int i, int* sc, int* m) {
+    if (i < 4) {
+        *sc = p[i] & 63;
+        *m = p[i + 4] & 63;
+    } else {
+        *sc = (p[i + 4] & 0xF) | ((p[i - 4] >> 6) << 4);
+        *m = (p[i + 4] >> 4) | ((p[i] >> 6) << 4);
+    }
+}
+
+// The linear-order word (k0 + e at nibble e) of column `col`, k0 % 8 == 0: eight
+// consecutive k sit in one half of one quarter, i.e. in 8 consecutive code bytes.
+HQ_HD uint32_t q4k_linear_word(const uint8_t* w, int K, int col, int k0) {
+    const uint8_t* blk = w + ((size_t)col * (size_t)(K / 256) + (size_t)(k0 / 256)) * kQ4KBlockBytes;
+    const int within = k0 % 256, l = within % 64;
+    const uint8_t* q = blk + 16 + 32 * (within / 64) + (l & 31);
+    const int shift = l >= 32 ? 4 : 0;
+    uint32_t lin = 0;
+    for (int e = 0; e < 8; ++e) lin |= (uint32_t)((q[e] >> shift) & 0xF) << (4 * e);
+    return lin;
+}
+
+// Scale and bias of (sub-block row g = k / 32, column n).
+HQ_HD void q4k_scale_bias(const uint8_t* w, int K, int g, int n, float* scale, float* bias) {
+    const uint8_t* blk = w + ((size_t)n * (size_t)(K / 256) + (size_t)(g / 8)) * kQ4KBlockBytes;
+    int sc, m;
+    q4k_scale_min(blk + 4, g % 8, &sc, &m);
+    const float d = half_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+    const float dmin = half_bits_to_f32((uint32_t)blk[2] | ((uint32_t)blk[3] << 8));
+    *scale = d * (float)sc;
+    *bias = -(dmin * (float)m);
+}
+
+// Tile word i (storage order) -> its column and first k.
+HQ_HD void tile_word_coords(const TileGeom& geo, size_t i, int* col, int* k0) {
+    const size_t chunk = i / 128;  // int4: 32 lanes x 4 words per chunk
+    const int within = (int)(i % 128);
+    const int lane = within / 4, j = within % 4;
+    const size_t per_full_group = (size_t)kGroupStrips * geo.KB;
+    const int sg = (int)(chunk / per_full_group);
+    const size_t rem = chunk - (size_t)sg * per_full_group;
+    const int w = geo.width(sg);
+    const int kb = (int)(rem / w), sl = (int)(rem % w);
+    int kw;
+    tile_word_source(4, sg * kGroupStrips + sl, kb, lane, j, col, &kw);
+    *k0 = kw * 8;
+}
+
+__global__ void q4k_to_tile_kernel(const uint8_t* __restrict__ w, uint32_t* __restrict__ tile,
+                                   float* __restrict__ scales, float* __restrict__ bias, int K, int N) {
+    const TileGeom geo(K, N, 4);
+    const size_t words = geo.bytes() / 4, rows = (size_t)(K / 32) * N;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < words; i += stride) {
+        int col, k0;
+        tile_word_coords(geo, i, &col, &k0);
+        tile[i] = u4_linear_to_tile(q4k_linear_word(w, K, col, k0));
+    }
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < rows; i += stride) {
+        const int n = (int)(i % N), g = (int)(i / N);  // n fastest: coalesced rows
+        q4k_scale_bias(w, K, g, n, scales + i, bias + i);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_q4k_to_tile(const uint8_t* w, uint8_t* tile, float* scales, float* bias, int K, int N,
+                               cudaStream_t s) {
+    const TileGeom geo(K, N, 4);
+    q4k_to_tile_kernel<<<grid_for(geo.bytes() / 4), 256, 0, s>>>(w, reinterpret_cast<uint32_t*>(tile), scales, bias,
+                                                                 K, N);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_linear_to_tile(const void* src, bool src_is_quad, int wbits, uint8_t* dst, int K, int N,
                                   cudaStream_t s) {
@@ -173,6 +290,20 @@ void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N,
             const uint32_t v = src[i];
             dst[(size_t)kw * N + col] = wbits == 4 ? u4_tile_to_linear(v) : t2_tile_to_linear(v);
         }
+    });
+}
+
+void q4k_to_tile(const uint8_t* w, uint32_t* tile, float* scales, float* bias, int K, int N, int nthreads) {
+    const TileGeom geo(K, N, 4);
+    parallel_for(geo.bytes() / 4, nthreads, [&](size_t a, size_t b) {
+        for (size_t i = a; i < b; ++i) {
+            int col, k0;
+            tile_word_coords(geo, i, &col, &k0);
+            tile[i] = u4_linear_to_tile(q4k_linear_word(w, K, col, k0));
+        }
+    });
+    parallel_for((size_t)(K / 32) * N, nthreads, [&](size_t a, size_t b) {
+        for (size_t i = a; i < b; ++i) q4k_scale_bias(w, K, (int)(i / N), (int)(i % N), scales + i, bias + i);
     });
 }
 

@@ -22,7 +22,7 @@ from ._lib import (HQ_BF16, HQ_F16, HQ_F32, HQ_WFMT_LINEAR_T2, HQ_WFMT_LINEAR_U4
                    HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TQ1_0, HQError, check, lib)
 
 __all__ = ["HQError", "weight_bytes", "repack_host", "repack", "make_workspace", "gemm", "QuantLinear",
-           "tq1_0_gemv", "tq1_0_to_tile_t2", "output_projection", "embedding_lookup", "w8_gemm", "check_device_error",
+           "tq1_0_gemv", "tq1_0_to_tile_t2", "q4_k_to_tile_u4", "q4_k_to_tile_u4_host", "output_projection", "embedding_lookup", "w8_gemm", "check_device_error",
            "MarlinGemmEngine",
            "HQ_WFMT_LINEAR_U4", "HQ_WFMT_MARLIN_QUAD", "HQ_WFMT_TILE_U4", "HQ_WFMT_LINEAR_T2",
            "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0"]
@@ -164,6 +164,28 @@ def tq1_0_to_tile_t2(w: torch.Tensor, K: int, N: int, stream=None):
     scales = torch.empty((K // 128, N), dtype=torch.float16, device=w.device)
     check(lib().hq_tq1_0_to_tile_t2(_ptr(w), _ptr(tile), _ptr(scales), K, N, _stream(stream)))
     return tile, scales
+
+
+def q4_k_to_tile_u4(w: torch.Tensor, K: int, N: int, stream=None):
+    """GGUF Q4_K blocks [N][K/256] (uint8, device) -> (TILE_U4 codes, f32 scales [K/32, N],
+    f32 bias [K/32, N]) for gemm(..., bias=bias, group=32)."""
+    tile = torch.empty(weight_bytes(HQ_WFMT_TILE_U4, K, N), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((K // 32, N), dtype=torch.float32, device=w.device)
+    bias = torch.empty((K // 32, N), dtype=torch.float32, device=w.device)
+    check(lib().hq_q4_k_to_tile_u4(_ptr(w), _ptr(tile), _ptr(scales), _ptr(bias), K, N, _stream(stream)))
+    return tile, scales, bias
+
+
+def q4_k_to_tile_u4_host(w: np.ndarray, K: int, N: int, nthreads: int = 0):
+    """Host-thread form of q4_k_to_tile_u4 on numpy arrays."""
+    src = np.ascontiguousarray(w, dtype=np.uint8)
+    tile = np.empty(weight_bytes(HQ_WFMT_TILE_U4, K, N), np.uint8)
+    scales = np.empty((K // 32, N), np.float32)
+    bias = np.empty((K // 32, N), np.float32)
+    vp = ctypes.c_void_p
+    check(lib().hq_q4_k_to_tile_u4_host(src.ctypes.data_as(vp), tile.ctypes.data_as(vp), scales.ctypes.data_as(vp),
+                                        bias.ctypes.data_as(vp), K, N, nthreads))
+    return tile, scales, bias
 
 
 def check_device_error() -> None:

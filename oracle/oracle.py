@@ -293,6 +293,75 @@ def max_rel_err(y, y_ref) -> float:
     return float(np.max(np.abs(y - y_ref)) / (den if den > 0 else 1.0))
 
 
+# --------------------------------------------------------------- GGUF Q4_K
+#
+# The reference names Q4_K only as a GGUF block type (hydrogen/include/
+# gguf_parser.hpp:44 type 12, :130 256 weights in 144 bytes); its field layout
+# and dequantisation are llama.cpp's (ggml/src/ggml-common.h block_q4_K,
+# ggml/src/ggml-quants.c dequantize_row_q4_K / get_scale_min_k4), a pinned but
+# un-vendored dependency of the reference.  Restated here from that published
+# format; pinned against gguf-py 0.19.0 (gguf.quants.dequantize, llama.cpp's own
+# Python copy of the format) by tests/golden/make_q4k_golden.py.
+
+Q4K_BLOCK_BYTES = 144
+
+
+def unpack_q4_k(blob: np.ndarray, K: int, N: int):
+    """Q4_K blocks [N][K/256] -> (codes u uint8 [K][N], scale f32 [K/32][N], bias f32 [K/32][N])
+    with weight = u * scale + bias, scale = d * sc_i, bias = -(dmin * m_i)."""
+    nb = K // 256
+    blk = np.ascontiguousarray(blob, np.uint8).reshape(N, nb, Q4K_BLOCK_BYTES)
+    d = blk[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)        # [N, nb]
+    dmin = blk[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    p = blk[:, :, 4:16].astype(np.int32)                                         # [N, nb, 12]
+    sc = np.empty((N, nb, 8), np.int32)
+    mn = np.empty((N, nb, 8), np.int32)
+    sc[..., 0:4] = p[..., 0:4] & 63
+    mn[..., 0:4] = p[..., 4:8] & 63
+    sc[..., 4:8] = (p[..., 8:12] & 0xF) | ((p[..., 0:4] >> 6) << 4)
+    mn[..., 4:8] = (p[..., 8:12] >> 4) | ((p[..., 4:8] >> 6) << 4)
+    qs = blk[:, :, 16:].reshape(N, nb, 4, 32)
+    codes = np.stack([qs & 0xF, qs >> 4], axis=3).reshape(N, K)                  # k = 64j + 32h + l
+    scale = (d[:, :, None] * sc.astype(np.float32)).reshape(N, K // 32)
+    bias = -(dmin[:, :, None] * mn.astype(np.float32)).reshape(N, K // 32)
+    return (np.ascontiguousarray(codes.T), np.ascontiguousarray(scale.T.astype(np.float32)),
+            np.ascontiguousarray(bias.T.astype(np.float32)))
+
+
+def dequant_q4_k(blob: np.ndarray, K: int, N: int) -> np.ndarray:
+    """llama.cpp's dequantize_row_q4_K per row, as float32 [K][N]: y = (d sc) u - dmin m."""
+    u, scale, bias = unpack_q4_k(blob, K, N)
+    s = np.repeat(scale, 32, axis=0)
+    m = -np.repeat(bias, 32, axis=0)
+    return (s * u.astype(np.float32)).astype(np.float32) - m
+
+
+def q4_k_to_tile(blob: np.ndarray, K: int, N: int):
+    """The oracle's Q4_K -> (TILE_U4 bytes, scale, bias): the tile packer on q = u - 8."""
+    u, scale, bias = unpack_q4_k(blob, K, N)
+    return pack_tile(u.astype(np.int8) - 8, 4), scale, bias
+
+
+def q4_k_gemm(X, blob, K, N, nthreads=0):
+    """X [M][K] fp32 times the Q4_K weights, through the fused int4 oracle (group 32, biased form)."""
+    u, scale, bias = unpack_q4_k(blob, K, N)
+    linear = pack_linear_u4(u.astype(np.int8) - 8)
+    return w4_gemm(X, linear, scale, bias, group=32, nthreads=nthreads)
+
+
+def gen_q4_k_blocks(K: int, N: int, seed: int = 0, d_range=(1e-3, 4e-3), dmin_range=(1e-3, 4e-3)) -> np.ndarray:
+    """Seeded Q4_K tensor [N][K/256] of 144-byte blocks: random scale/min/code bytes and
+    fp16 d / dmin drawn uniformly from the given ranges (weights of order 0.1)."""
+    rng = np.random.default_rng(seed)
+    nb = K // 256
+    blk = rng.integers(0, 256, size=(N, nb, Q4K_BLOCK_BYTES), dtype=np.uint8)
+    d = rng.uniform(*d_range, size=(N, nb)).astype(np.float16)
+    dmin = rng.uniform(*dmin_range, size=(N, nb)).astype(np.float16)
+    blk[:, :, 0:2] = d.view(np.uint8).reshape(N, nb, 2)
+    blk[:, :, 2:4] = dmin.view(np.uint8).reshape(N, nb, 2)
+    return blk.reshape(-1)
+
+
 # ----------------------------------------------------- reference (compiled)
 
 def ref_repack_q4k_to_marlin(linear: np.ndarray, K: int, N: int):

@@ -120,7 +120,9 @@ def test_gemm_argument_errors_need_no_device():
                                a["ct"], a["M"], a["N"], a["K"], a["g"], a["ws"], a["wsb"], a["stream"])
     assert call(args(N=24)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
     assert call(args(K=96)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
-    assert call(args(g=32)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert call(args(g=16)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE  # groups: 32 or multiples of 64
+    assert call(args(g=96, K=192)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
+    assert call(args(g=32, K=96)) == _lib.HQ_ERR_UNSUPPORTED_SHAPE
     assert call(args(M=-1)) == _lib.HQ_ERR_INVALID_ARG
     assert call(args(at=7)) == _lib.HQ_ERR_INVALID_ARG
     assert call(args(wf=_lib.HQ_WFMT_TQ1_0)) == _lib.HQ_ERR_INVALID_ARG

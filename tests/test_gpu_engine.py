@@ -85,10 +85,11 @@ def _ref():
 
 
 @pytest.mark.parametrize("M", [1, 2, 4, 8])
-def test_oracle_pinned_to_reference_kernels(M):
+@pytest.mark.parametrize("g", [128, 32])
+def test_oracle_pinned_to_reference_kernels(M, g):
     r = _ref()
-    K, N, g = 512, 256, 128  # the reference's split-K needs K % 512 == 0 (marlin_gemm.cu:156-159)
-    X, S, B, lin = ref_case(M, K, N, g, seed=10 + M)
+    K, N = 512, 256  # the reference's split-K needs K % 512 == 0 and group % 32 == 0 (marlin_gemm.cu:156-159)
+    X, S, B, lin = ref_case(M, K, N, g, seed=10 + M + g)
     quad = o.repack_marlin_quad(lin, K, N)
     W = o.dequant_u4(lin, S, B, K, N, g)
     h = r.ref_engine_create(8, K, N, g)
@@ -103,5 +104,40 @@ def test_oracle_pinned_to_reference_kernels(M):
         assert np.array_equal(Yr.cpu().numpy(), o.gemm_f32(X, W))
         # the reference's own Marlin kernel meets its bound against the oracle
         assert np.max(np.abs(Ym.cpu().numpy() - o.w4_gemm(X, lin, S, B, group=g))) < 1e-3
+    finally:
+        r.ref_engine_destroy(ctypes.c_void_p(h))
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 13])
+def test_engine_group32_against_reference_kernel(M):
+    """Group 32, which the reference's Marlin engine accepts (group % 32 == 0): the drop-in's
+    forward_marlin_int4 and the reference's own kernel on identical inputs, both within the
+    reference's 1e-3 bound of the oracle."""
+    K, N, g = 1024, 256, 32
+    X, S, B, lin = ref_case(M, K, N, g, seed=40 + M)
+    quad = o.repack_marlin_quad(lin, K, N)
+    ref = o.w4_gemm(X, lin, S, B, group=g)
+    dX, dQ, dS, dB = dev(X), dev(quad), dev(S), dev(B)
+    eng = hq.MarlinGemmEngine(max(M, 8), K, N, g)
+    Ym = torch.zeros((M, N), device="cuda")
+    eng.forward_marlin_int4(dX, dQ, dS, dB, Ym, M)
+    torch.cuda.synchronize()
+    ours = Ym.cpu().numpy()
+    assert np.max(np.abs(ours - ref)) < 1e-3
+    assert o.max_rel_err(ours, ref) <= 1e-5
+    eng.close()
+    # the reference's kernels hold at most 8 rows (acc[8], marlin_gemm.cu:260): no M > 8 there
+    if o.ref_lib() is None or M > 8:
+        return
+    r = _ref()
+    h = r.ref_engine_create(8, K, N, g)
+    assert h, r.ref_last_error()
+    try:
+        Yr = torch.zeros((M, N), device="cuda")
+        assert r.ref_forward_marlin(ctypes.c_void_p(h), P(dX), P(dQ), P(dS), P(dB), P(Yr), M) == 0
+        torch.cuda.synchronize()
+        theirs = Yr.cpu().numpy()
+        assert np.max(np.abs(theirs - ref)) < 1e-3
+        assert np.max(np.abs(ours - theirs)) < 1e-3
     finally:
         r.ref_engine_destroy(ctypes.c_void_p(h))
