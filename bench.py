@@ -549,7 +549,8 @@ def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
 
 def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
     """GGUF Q4_K at model load: hq_q4_k_to_tile_u4 (GB/s of Q4_K blocks in) and the group-32 GEMM it
-    feeds (fp16 activations, f32 scale and bias rows per 32 weights) at the 27B shapes, M in {1, 16}.
+    feeds (fp16 activations, f32 scale and bias rows per 32 weights) at the 27B shapes, M in {1, 16}
+    (decode kernel) and M = 2048 (tcgen05 kernel, TFLOP/s).
     Decode GB/s counts the bytes the kernel must read: codes (K N / 2) plus 8 bytes of scale and bias
     per 32 weights, activations and outputs."""
     import ctypes
@@ -558,7 +559,7 @@ def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
     g.manual_seed(77)
     half_bits = torch.tensor([0.002], dtype=torch.float16).view(torch.uint8).to(dev)  # d = dmin = 0.002
     rows, conv = [], []
-    dec_bytes, dec_ms = 0.0, 0.0
+    dec_bytes, dec_ms, pf_flop, pf_ms = 0.0, 0.0, 0.0, 0.0
     for name, K, N in SHAPES:
         nblk = N * (K // 256)
         copies = []
@@ -581,7 +582,7 @@ def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
         conv.append({"shape": name, "K": K, "N": N, "us": round(ms * 1e3, 1),
                      "GBps_in": round(nblk * 144 / (ms / 1e3) / 1e9, 1)})
         copies = [(t, s, b) for (_, t, s, b) in copies]
-        for M in (1, 16):
+        for M in (1, 16, 2048):
             A = torch.randn((M, K), device=dev, generator=g).half()
             C = torch.empty((M, N), device=dev, dtype=torch.float16)
             nb = int(L.hq_gemm_workspace_size(M, N, K, 32, _lib.HQ_WFMT_TILE_U4))
@@ -594,18 +595,26 @@ def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
                                vp(ws.data_ptr()), ws.numel(), vp(stream.cuda_stream))
                 if st != 0:
                     raise RuntimeError(L.hq_last_error_string().decode())
-            ms = _time_launches(torch, stream, fn, len(copies), reps=20)
-            nbytes = K * N // 2 + 2 * (K // 32) * N * 4 + M * K * 2 + M * N * 2
-            dec_bytes += nbytes
-            dec_ms += ms
-            rows.append({"shape": name, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
-                         "GBps": round(nbytes / (ms / 1e3) / 1e9, 1)})
+            ms = _time_launches(torch, stream, fn, len(copies), reps=20 if M <= 16 else 10)
+            row = {"shape": name, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2)}
+            if M <= 16:
+                nbytes = K * N // 2 + 2 * (K // 32) * N * 4 + M * K * 2 + M * N * 2
+                dec_bytes += nbytes
+                dec_ms += ms
+                row["GBps"] = round(nbytes / (ms / 1e3) / 1e9, 1)
+            else:
+                pf_flop += 2.0 * M * N * K
+                pf_ms += ms
+                row["TFLOPS"] = round(2.0 * M * N * K / (ms / 1e3) / 1e12, 1)
+            rows.append(row)
             del A, C, ws
         del copies
     dec = dec_bytes / (dec_ms / 1e3) / 1e9
-    return {"metric": "GGUF Q4_K: load-time conversion and group-32 decode GEMM",
-            "decode_GBps": dec, "decode_frac_hbm": dec / peaks["hbm_gbs"], "dtype": "f16",
-            "timing": "per call: CUDA events around 20 GEMMs / 10 conversions queued behind a spin kernel, after "
+    pf = pf_flop / (pf_ms / 1e3) / 1e12
+    return {"metric": "GGUF Q4_K: load-time conversion and group-32 GEMM",
+            "decode_GBps": dec, "decode_frac_hbm": dec / peaks["hbm_gbs"],
+            "prefill_TFLOPS": pf, "prefill_frac_tensor": pf / peaks["bf16_tflops"], "dtype": "f16",
+            "timing": "per call: CUDA events around 20 (M<=16) / 10 GEMMs, 10 conversions, queued behind a spin kernel, after "
                       "3 warm-up, rotating weight copies (not graph-captured)",
             "conversion": conv, "per_gemm": rows}
 

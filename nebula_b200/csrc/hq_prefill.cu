@@ -56,13 +56,16 @@ constexpr uint32_t kColA = 256;  // A ring: kColA + 32 * buf
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int WBITS>
+// kF32S: f32 scale rows (int4 only): per k-block the scale rows of its two
+// 32-k halves, then their bias rows (any group of 32 or a multiple of 64).
+template <int WBITS, bool kF32S = false>
 struct TsLayout {
     static constexpr int kCB = WBITS == 4 ? 512 : 256;
     static constexpr int kX = TN * BK * 2;                 // activation tile, 1024-aligned at stage start
     static constexpr int kCodes = kGroupStrips * kCB;      // one strip group x 64 k
-    static constexpr int kScale = TM * 2;
+    static constexpr int kScale = kF32S ? 4 * TM * 4 : TM * 2;
     static constexpr int kStage = align_up(kX + kCodes + kScale, 1024);
+    static constexpr int kStages = kF32S ? 5 : hq::kStages;  // six 38 KB stages exceed 227 KB
     static constexpr int kRing = kStages * kStage;
     static constexpr int kSmem = kRing + 256 + 1024;      // barriers + TMEM slot + alignment slack
 };
@@ -71,6 +74,7 @@ struct alignas(64) PrefillTsParams {
     CUtensorMap x_map;  // [M][K] 16-bit: box 64 x 256, 128B swizzle, rows >= M read zero
     const uint8_t* W;
     const void* S;
+    const float* bias;  // f32-scale kernels only; nullable (then w = (u - 8) s)
     void* C;
     unsigned* err;
     int M, N, K, group;
@@ -87,9 +91,29 @@ __device__ __forceinline__ OT cvt_out(float v) {
     return from_f32<OT>(v);
 }
 
-template <int WBITS, typename T, typename OT>
+// f32-scale form: the codes at bit offsets `shift` and `shift + 16` of a tile
+// word (one k pair) as u * s + b in fp32, rounded once to the operand type.
+// u comes exact from the 2^23 mantissa trick.
+template <bool kBF16>
+__device__ __forceinline__ uint32_t affine_pair(uint32_t w, int shift, float s, float b) {
+    const float ua = __uint_as_float(0x4B000000u | ((w >> shift) & 0xFu)) - 8388608.f;
+    const float ub = __uint_as_float(0x4B000000u | ((w >> (shift + 16)) & 0xFu)) - 8388608.f;
+    const float lo = fmaf(ua, s, b), hi = fmaf(ub, s, b);
+    uint32_t r;
+    if constexpr (kBF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        r = *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(lo, hi);
+        r = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return r;
+}
+
+template <int WBITS, typename T, typename OT, bool kF32S>
 __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_constant__ PrefillTsParams p) {
-    using L = TsLayout<WBITS>;
+    using L = TsLayout<WBITS, kF32S>;
+    constexpr int kStages = L::kStages;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr int kCB = L::kCB;
     constexpr uint32_t kIdesc = umma_idesc_f16(kBF16, TM, TN);
@@ -143,18 +167,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                 const int mt = tile % p.m_tiles, sg = tile / p.m_tiles;
                 const int width = geo.width(sg);
                 const uint32_t unit_bytes = (uint32_t)width * kCB;
-                const uint32_t s_bytes = (uint32_t)width * kStripCols * 2;
+                const uint32_t s_bytes = (uint32_t)width * kStripCols * (kF32S ? 4 : 2);
+                const uint32_t srows = kF32S ? (p.bias ? 4u : 2u) : 1u;
                 const size_t off = geo.unit_offset((long long)sg * KB);
                 for (int kb = 0; kb < KB; ++kb, ++it) {
                     const int slot = it % kStages;
                     if (ok) ok = mbar_wait(&empty[slot], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.err);
                     uint8_t* st = ring + slot * L::kStage;
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)L::kX + unit_bytes + s_bytes);
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t)L::kX + unit_bytes + srows * s_bytes);
                     tma_load_2d(st, &p.x_map, kb * BK, mt * TN, &full[slot]);
                     bulk_g2s_hint(st + L::kX, p.W + off + (size_t)kb * unit_bytes, unit_bytes, &full[slot], pol);
-                    const int gi = kb * BK / p.group;
-                    bulk_g2s(st + L::kX + L::kCodes, Sb + ((size_t)gi * p.N + (size_t)sg * TM) * 2, s_bytes,
-                             &full[slot]);
+                    if constexpr (kF32S) {
+                        // rows of the block's two 32-k halves (the same row twice when group >= 64)
+                        const uint8_t* Bb = reinterpret_cast<const uint8_t*>(p.bias);
+                        for (int h = 0; h < 2; ++h) {
+                            const size_t o = ((size_t)((kb * BK + 32 * h) / p.group) * p.N + (size_t)sg * TM) * 4;
+                            bulk_g2s(st + L::kX + L::kCodes + h * TM * 4, Sb + o, s_bytes, &full[slot]);
+                            if (Bb) bulk_g2s(st + L::kX + L::kCodes + (2 + h) * TM * 4, Bb + o, s_bytes, &full[slot]);
+                        }
+                    } else {
+                        const int gi = kb * BK / p.group;
+                        bulk_g2s(st + L::kX + L::kCodes, Sb + ((size_t)gi * p.N + (size_t)sg * TM) * 2, s_bytes,
+                                 &full[slot]);
+                    }
                 }
             }
             // Copies still in flight land before the CTA exits.
@@ -212,9 +247,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                 const uint8_t* st = ring + slot * L::kStage;
                 const uint8_t* codes = st + L::kX + sl * kCB;
                 uint32_t s2 = 0u;
+                float sv[2] = {0.f, 0.f}, bv[2] = {0.f, 0.f};  // f32 form: per 32-k half
                 if (valid) {
-                    const uint32_t v = *reinterpret_cast<const uint16_t*>(st + L::kX + L::kCodes + 2 * cl);
-                    s2 = v | (v << 16);
+                    if constexpr (kF32S) {
+                        const float* sr = reinterpret_cast<const float*>(st + L::kX + L::kCodes);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            sv[h] = sr[h * TM + cl];
+                            bv[h] = p.bias ? sr[(2 + h) * TM + cl] : -8.f * sv[h];
+                        }
+                    } else {
+                        const uint32_t v = *reinterpret_cast<const uint16_t*>(st + L::kX + L::kCodes + 2 * cl);
+                        s2 = v | (v << 16);
+                    }
                 }
                 const uint32_t ta = tmem + lane_base + kColA + 32u * ab;
                 uint32_t cw[WBITS == 4 ? 8 : 4];  // this column's codes, k order
@@ -223,7 +268,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     uint32_t r[8];
-                    if constexpr (WBITS == 4) {
+                    if constexpr (kF32S) {
+                        // k 16t .. 16t+15 lie in half t / 2; pairs (e0,e1) (e2,e3) (e4,e5) (e6,e7)
+                        // of a word sit at bit offsets 0, 8, 4, 12 (and +16)
+                        const float s = sv[t >> 1], b = bv[t >> 1];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int sh = e == 0 ? 0 : e == 1 ? 8 : e == 2 ? 4 : 12;
+                            r[e] = affine_pair<kBF16>(cw[2 * t], sh, s, b);
+                            r[4 + e] = affine_pair<kBF16>(cw[2 * t + 1], sh, s, b);
+                        }
+                    } else if constexpr (WBITS == 4) {
                         const uint2 w = make_uint2(cw[2 * t], cw[2 * t + 1]);
                         uint32_t lo[4], hi[4];
                         if constexpr (kBF16) {
@@ -542,14 +597,29 @@ using PrefillTsFn = void (*)(PrefillTsParams);
 
 template <int WBITS, typename T, bool PAIR>
 PrefillTsFn ts_pick_out(DType c) {
-    if (c == DType::F32) return PAIR ? prefill_pair_kernel<WBITS, T, float> : prefill_ts_kernel<WBITS, T, float>;
+    if (c == DType::F32) return PAIR ? prefill_pair_kernel<WBITS, T, float> : prefill_ts_kernel<WBITS, T, float, false>;
     if ((std::is_same<T, __half>::value && c == DType::F16) || (std::is_same<T, __nv_bfloat16>::value && c == DType::BF16))
-        return PAIR ? prefill_pair_kernel<WBITS, T, T> : prefill_ts_kernel<WBITS, T, T>;
+        return PAIR ? prefill_pair_kernel<WBITS, T, T> : prefill_ts_kernel<WBITS, T, T, false>;
+    return nullptr;
+}
+
+// f32 scale rows (int4, one-CTA kernel): group 32 or a multiple of 64; with a
+// bias for fp16 activations, without one for bf16 (as the decode kernels).
+template <typename T>
+PrefillTsFn ts_pick_f32s(DType c) {
+    if (c == DType::F32) return prefill_ts_kernel<4, T, float, true>;
+    if ((std::is_same<T, __half>::value && c == DType::F16) || (std::is_same<T, __nv_bfloat16>::value && c == DType::BF16))
+        return prefill_ts_kernel<4, T, T, true>;
     return nullptr;
 }
 
 template <bool PAIR>
 PrefillTsFn ts_select(const GemmArgs& a) {
+    if (!PAIR && a.wbits == 4 && a.s_dtype == DType::F32 && (a.group == 32 || a.group % BK == 0)) {
+        if (a.a_dtype == DType::F16) return ts_pick_f32s<__half>(a.c_dtype);
+        if (a.a_dtype == DType::BF16 && !a.bias) return ts_pick_f32s<__nv_bfloat16>(a.c_dtype);
+        return nullptr;
+    }
     if (a.bias || a.s_dtype != a.a_dtype || a.group % BK) return nullptr;
     if (a.a_dtype == DType::F16)
         return a.wbits == 4 ? ts_pick_out<4, __half, PAIR>(a.c_dtype) : ts_pick_out<2, __half, PAIR>(a.c_dtype);
@@ -574,11 +644,12 @@ cudaError_t launch_prefill(const GemmArgs& a) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const bool pair = HQ_PREFILL_PAIR != 0 && a.K % (2 * BK) == 0;
+    const bool pair = HQ_PREFILL_PAIR != 0 && a.K % (2 * BK) == 0 && ts_select<true>(a) != nullptr;
+    const bool f32s = a.s_dtype == DType::F32;
     PrefillTsFn fn = pair ? ts_select<true>(a) : ts_select<false>(a);
     if (!fn) return cudaErrorInvalidValue;
     const int smem = pair ? (a.wbits == 4 ? PairLayout<4>::kSmem : PairLayout<2>::kSmem)
-                          : (a.wbits == 4 ? TsLayout<4>::kSmem : TsLayout<2>::kSmem);
+                          : (f32s ? TsLayout<4, true>::kSmem : a.wbits == 4 ? TsLayout<4>::kSmem : TsLayout<2>::kSmem);
     e = ensure_smem_attr(reinterpret_cast<const void*>(fn), dev, smem);
     if (e != cudaSuccess) return e;
     PrefillTsParams p;
@@ -589,6 +660,7 @@ cudaError_t launch_prefill(const GemmArgs& a) {
     if (e != cudaSuccess) return e;
     p.W = a.W;
     p.S = a.S;
+    p.bias = a.bias;
     p.C = a.C;
     p.err = device_error_word(dev);
     p.M = a.M;

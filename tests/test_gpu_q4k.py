@@ -56,11 +56,11 @@ def q4k_case(M, K, N, seed, a_dtype):
     return blob, X
 
 
-@pytest.mark.parametrize("M", [1, 2, 5, 8, 9, 16, 40])
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 9, 16])
 @pytest.mark.parametrize("a_dtype", ["f16", "f32"])
 def test_q4_k_gemm_parity(M, a_dtype):
-    """Q4_K blocks -> device conversion -> hq_gemm(group 32, f32 scale and bias) against the
-    fused oracle; M = 40 runs as three 16-row launches.  N = 272 leaves a one-strip group."""
+    """Q4_K blocks -> device conversion -> hq_gemm(group 32, f32 scale and bias) on the decode
+    kernel against the fused oracle.  N = 272 leaves a one-strip group."""
     K, N = 1024, 272
     blob, X = q4k_case(M, K, N, 100 + M, a_dtype)
     ref = o.q4_k_gemm(X, blob, K, N)
@@ -81,16 +81,67 @@ def test_q4_k_gemm_parity(M, a_dtype):
     assert np.max(np.abs(y - y64)) <= 1e-4 * np.max(np.abs(y64))
 
 
-@pytest.mark.parametrize("M", [1, 16])
+def rounded_weight_ref(X, u, scale, bias, dtype):
+    """float64 product with the weights u * s + b rounded to the tensor-core operand type, as the
+    prefill kernel's dequantiser forms them (fp32 fma, one rounding)."""
+    g = u.shape[0] // scale.shape[0]
+    s = np.repeat(scale.astype(np.float64), g, axis=0)
+    b = np.repeat(bias.astype(np.float64), g, axis=0)
+    W = o.round_to((u.astype(np.float64) * s + b).astype(np.float32), dtype).astype(np.float64)
+    return X.astype(np.float64) @ W
+
+
+@pytest.mark.parametrize("M", [17, 40, 300])
+def test_q4_k_prefill(M):
+    """M > 16: the tcgen05 kernel's f32-scale form (two scale and bias rows per 64-k block)."""
+    K, N = 1024, 272
+    blob, X = q4k_case(M, K, N, 200 + M, "f16")
+    tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
+    Xt = torch.from_numpy(X).to("cuda:0").half()
+    y = hq.gemm(Xt, tile, s, N=N, group=32, bias=b, out_dtype=torch.float32).cpu().numpy()
+    hq.check_device_error()
+    u, scale, bias = o.unpack_q4_k(blob, K, N)
+    assert o.max_rel_err(y, rounded_weight_ref(X, u, scale, bias, "f16")) <= 1e-5
+    assert o.max_rel_err(y, o.q4_k_gemm(X, blob, K, N)) <= TOL16["f16"]
+    y16 = hq.gemm(Xt, tile, s, N=N, group=32, bias=b).float().cpu().numpy()
+    assert o.max_rel_err(y16, o.q4_k_gemm(X, blob, K, N)) <= TOL16["f16"]
+    y2 = hq.gemm(Xt, tile, s, N=N, group=32, bias=b, out_dtype=torch.float32).cpu().numpy()
+    assert np.array_equal(y, y2)
+
+
+@pytest.mark.parametrize("M,K,N,g", [(64, 512, 144, 32), (200, 1024, 272, 128), (130, 768, 256, 64)])
+@pytest.mark.parametrize("a_dtype,with_bias", [("f16", True), ("f16", False), ("bf16", False)])
+def test_prefill_f32_scales(M, K, N, g, a_dtype, with_bias):
+    """f32 scale rows (and the reference's bias form) at M > 16 with 16-bit activations: group 32
+    and groups of 64 / 128 on the one-CTA tcgen05 kernel."""
+    rng = np.random.default_rng(M + K + g)
+    A, q, _ = o.gen_int4_case(M, K, N, group=g, seed=M + N, a_dtype=a_dtype)
+    S = (0.005 + rng.random((K // g, N)) * 0.015).astype(np.float32)
+    B = (-8.0 * S + 0.01 * rng.standard_normal(S.shape)).astype(np.float32) if with_bias else None
+    W = dev_u8(o.pack_tile(q, 4))
+    At = torch.from_numpy(A).to("cuda:0").to(TDT[a_dtype])
+    Bt = torch.from_numpy(B).to("cuda:0") if with_bias else None
+    y = hq.gemm(At, W, torch.from_numpy(S).to("cuda:0"), N=N, group=g, bias=Bt, out_dtype=torch.float32)
+    y = y.cpu().numpy()
+    hq.check_device_error()
+    u = (q.astype(np.int16) + 8).astype(np.uint8)
+    bias = B if with_bias else (-8.0 * S).astype(np.float32)
+    assert o.max_rel_err(y, rounded_weight_ref(A, u, S, bias, a_dtype)) <= 1e-5
+    ref = o.w4_gemm(A, o.pack_linear_u4(q), S, B, group=g)
+    assert o.max_rel_err(y, ref) <= TOL16[a_dtype]
+
+
+@pytest.mark.parametrize("M", [1, 16, 2048])
 def test_q4_k_27b_qkv_shape(M):
     """The 27B QKV projection (K 5120, N 7168) held as Q4_K."""
     K, N = 5120, 7168
     blob, X = q4k_case(M, K, N, 7 + M, "f16")
-    ref = o.q4_k_gemm(X, blob, K, N)
+    rows = np.arange(M) if M <= 16 else np.arange(0, M, 61)  # sampled rows at M = 2048
+    ref = o.q4_k_gemm(X[rows], blob, K, N)
     tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
     y = hq.gemm(torch.from_numpy(X).to("cuda:0").half(), tile, s, N=N, group=32, bias=b,
                 out_dtype=torch.float32).cpu().numpy()
-    assert o.max_rel_err(y, ref) <= 1e-4
+    assert o.max_rel_err(y[rows], ref) <= (1e-4 if M <= 16 else TOL16["f16"])
 
 
 @pytest.mark.parametrize("M", [1, 8, 16, 33])
@@ -104,7 +155,12 @@ def test_group32_symmetric(M, a_dtype):
     At = torch.from_numpy(A).to("cuda:0").to(TDT[a_dtype])
     St = torch.from_numpy(S).to("cuda:0")
     y = hq.gemm(At, W, St, N=N, group=32, out_dtype=torch.float32).cpu().numpy()
-    assert o.max_rel_err(y, ref) <= 1e-4
+    if M > 16 and a_dtype != "f32":  # tcgen05 kernel: weights rounded to the operand type
+        u = (q.astype(np.int16) + 8).astype(np.uint8)
+        assert o.max_rel_err(y, rounded_weight_ref(A, u, S, (-8.0 * S).astype(np.float32), a_dtype)) <= 1e-5
+        assert o.max_rel_err(y, ref) <= TOL16[a_dtype]
+    else:
+        assert o.max_rel_err(y, ref) <= 1e-4
     if a_dtype != "f32":
         y16 = hq.gemm(At, W, St, N=N, group=32).float().cpu().numpy()
         assert o.max_rel_err(y16, ref) <= TOL16[a_dtype]
