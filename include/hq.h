@@ -128,7 +128,9 @@ HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t
  *            re-tiled into the workspace first (one extra pass over the
  *            weights); hq_gemm_workspace_size accounts for it.
  * M <= 16 runs the HBM-streaming decode kernel; larger M runs the tcgen05
- * tensor-core kernel.
+ * tensor-core kernel, which rounds each dequantised weight to the 16-bit
+ * activation type (with f32 scales: u * s + b formed in fp32, rounded once).
+ * f32 activations at M > 16 run the decode kernel 16 rows per launch.
  * Launch overlap (on by default, see hq_set_launch_overlap): a call may start
  * reading Wq and scales while the kernel enqueued just before it on the same
  * stream is still running (programmatic dependent launch); A is read only

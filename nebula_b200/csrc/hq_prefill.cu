@@ -91,23 +91,52 @@ __device__ __forceinline__ OT cvt_out(float v) {
     return from_f32<OT>(v);
 }
 
-// f32-scale form: the codes at bit offsets `shift` and `shift + 16` of a tile
-// word (one k pair) as u * s + b in fp32, rounded once to the operand type.
-// u comes exact from the 2^23 mantissa trick.
+// f32-scale form of one tile word: its k pairs (e0,e1) (e2,e3) (e4,e5) (e6,e7)
+// as u * s + b in fp32, rounded once to the operand type (fp32x2 arithmetic).
+// fp16 operands take u exactly as fp16 pairs from the shared dequantiser and
+// widen them on the FMA pipe.  bf16 operands OR each code field into the
+// mantissa of 2^23 (2^23 + u; a high-nibble field in place reads 2^23 + 16 u and
+// takes the exact scale s / 16), and one packed subtract gives the code.
 template <bool kBF16>
-__device__ __forceinline__ uint32_t affine_pair(uint32_t w, int shift, float s, float b) {
-    const float ua = __uint_as_float(0x4B000000u | ((w >> shift) & 0xFu)) - 8388608.f;
-    const float ub = __uint_as_float(0x4B000000u | ((w >> (shift + 16)) & 0xFu)) - 8388608.f;
-    const float lo = fmaf(ua, s, b), hi = fmaf(ub, s, b);
-    uint32_t r;
-    if constexpr (kBF16) {
-        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-        r = *reinterpret_cast<uint32_t*>(&v);
+__device__ __forceinline__ void affine_word(uint32_t w, float s, float b, uint32_t (&r)[4]) {
+    unsigned long long bb, ss;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(bb) : "f"(b));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
+    if constexpr (!kBF16) {
+        uint32_t uh[4];
+        dequant_u4_f16<true>(w, uh);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uh[p]));
+            unsigned long long v;
+            asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(u2.x), "f"(u2.y));
+            asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(v) : "l"(ss), "l"(bb));
+            float x, y;
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+            __half2 h = __floats2half2_rn(x, y);
+            r[p] = *reinterpret_cast<uint32_t*>(&h);
+        }
     } else {
-        __half2 v = __floats2half2_rn(lo, hi);
-        r = *reinterpret_cast<uint32_t*>(&v);
+        constexpr uint32_t kM = 0x4B000000u;  // 2^23
+        const uint32_t w8 = w >> 8, w16 = w >> 16, w24 = w >> 24;
+        const uint32_t lo[4] = {(w & 0xFu) | kM, (w8 & 0xFu) | kM, (w & 0xF0u) | kM, (w8 & 0xF0u) | kM};
+        const uint32_t hi[4] = {(w16 & 0xFu) | kM, (w24 & 0xFu) | kM, (w16 & 0xF0u) | kM, (w24 & 0xF0u) | kM};
+        const float s16 = s * 0.0625f;
+        unsigned long long mm, s16s;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(mm) : "r"(kM));
+        asm("mov.b64 %0, {%1, %1};" : "=l"(s16s) : "f"(s16));
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            unsigned long long v;
+            asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo[p]), "r"(hi[p]));
+            asm("sub.f32x2 %0, %0, %1;" : "+l"(v) : "l"(mm));
+            asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(v) : "l"(p < 2 ? ss : s16s), "l"(bb));
+            float x, y;
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+            __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+            r[p] = *reinterpret_cast<uint32_t*>(&h);
+        }
     }
-    return r;
 }
 
 template <int WBITS, typename T, typename OT, bool kF32S>
@@ -269,14 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                 for (int t = 0; t < 4; ++t) {
                     uint32_t r[8];
                     if constexpr (kF32S) {
-                        // k 16t .. 16t+15 lie in half t / 2; pairs (e0,e1) (e2,e3) (e4,e5) (e6,e7)
-                        // of a word sit at bit offsets 0, 8, 4, 12 (and +16)
+                        // k 16t .. 16t+15 lie in the block's 32-k half t / 2
                         const float s = sv[t >> 1], b = bv[t >> 1];
+                        uint32_t lo[4], hi[4];
+                        affine_word<kBF16>(cw[2 * t], s, b, lo);
+                        affine_word<kBF16>(cw[2 * t + 1], s, b, hi);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const int sh = e == 0 ? 0 : e == 1 ? 8 : e == 2 ? 4 : 12;
-                            r[e] = affine_pair<kBF16>(cw[2 * t], sh, s, b);
-                            r[4 + e] = affine_pair<kBF16>(cw[2 * t + 1], sh, s, b);
+                            r[e] = lo[e];
+                            r[4 + e] = hi[e];
                         }
                     } else if constexpr (WBITS == 4) {
                         const uint2 w = make_uint2(cw[2 * t], cw[2 * t + 1]);
