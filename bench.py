@@ -849,6 +849,12 @@ def main():
                     help="micro-batches of the TP stack at N > 1 (each step's rows split on 256-row tiles; two "
                          "measured slower at 2 GPUs: 1500 against 1760 TFLOP/s)")
     ap.add_argument("--ar-ctas", type=int, default=128, help="CTAs of hq_allreduce_sum in the TP stack")
+    ap.add_argument("--sweep-parallel", default="replicas", choices=["replicas", "tp"],
+                    help="decode sweep at N > 1.  'replicas': every GPU runs BASELINE configs[1] (a one-GPU "
+                         "workload) on its own weights, no collective (weak scaling; the units are all ranks' "
+                         "GEMMs).  'tp': its shapes sharded Megatron-style with an all-reduce after O and down "
+                         "(strong scaling; each shard is latency-bound).  The sharded multi-GPU workload of the "
+                         "north star is the layer stack, reported in tp_stack at every N.")
     ap.add_argument("--sweep-comm", default="nccl", choices=["hq", "nccl"],
                     help="all-reduce of the row-parallel outputs in the tensor-parallel decode sweep (10-160 KB "
                          "messages: NCCL measured faster than hq_allreduce_sum's two-barrier kernel there)")
@@ -881,16 +887,18 @@ def main():
     # ------------------------------------------------------------ workload
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
+    tpw = world if args.sweep_parallel == "tp" else 1  # tensor-parallel width of the decode sweep
+    replicas = world if args.sweep_parallel == "replicas" else 1
     gemms = []  # (name, M, K_local, N_local, allreduce)
     for M in MS:
         for name, K, N in SHAPES:
             if name in ("qkv", "gate_up"):
-                gemms.append((name, M, K, N // world, False))
+                gemms.append((name, M, K, N // tpw, False))
             else:
-                gemms.append((name, M, K // world, N, world > 1))
+                gemms.append((name, M, K // tpw, N, tpw > 1))
     weights = {}
     for name, K, N in SHAPES:
-        Kl, Nl = (K, N // world) if name in ("qkv", "gate_up") else (K // world, N)
+        Kl, Nl = (K, N // tpw) if name in ("qkv", "gate_up") else (K // tpw, N)
         copies = []
         for c in range(args.copies):
             W = torch.randint(0, 256, (hq.weight_bytes(_lib.HQ_WFMT_TILE_U4, Kl, Nl),), dtype=torch.uint8,
@@ -913,7 +921,7 @@ def main():
     # after each GEMM, by hq_allreduce_sum on PyTorch symmetric memory (epoch 0: the call
     # count lives in the flag area, so the calls replay inside the step's CUDA graph),
     # or by NCCL.
-    sweep_hq = world > 1 and args.sweep_comm == "hq"
+    sweep_hq = tpw > 1 and args.sweep_comm == "hq"
     ar_bufs = {}
     if sweep_hq:
         import torch.distributed._symmetric_memory as symm
@@ -1007,7 +1015,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     layer_bytes = sum(weight_bytes(K, N) for _, K, N in SHAPES)
-    step_bytes = layer_bytes * len(MS)
+    step_bytes = layer_bytes * len(MS) * replicas  # every rank's weight bytes (replicas: a full sweep each)
     value = step_bytes / (ms / 1e3) / 1e12
 
     # ----------------------------------------------- per-launch kernel timing
@@ -1130,13 +1138,16 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if args.sweep_parallel == "tp" else "weak",
             "vs_baseline": None, "dtype": "u4", "data": "synthetic (seeded random int4 codes, fp16 A ~N(0,1), "
                                                          "fp16 scales ~U(0.005,0.02))",
             "config": {"workload": "decode_sweep (BASELINE configs[1]): 27B layer QKV 5120x7168, O 5120x5120, "
                                    "gate_up 5120x34816, down 17408x5120 at M in {1,2,4,8,16}; int4 g128, fp16 A",
-                       "global_batch": "M in {1,2,4,8,16}", "parallelism": f"tp{world}" if world > 1 else "single",
-                       "collective": None if world == 1 else (
+                       "global_batch": "M in {1,2,4,8,16}" + (f" on each of {world} replicas" if replicas > 1 else ""),
+                       "parallelism": (f"tp{world}" if tpw > 1 else f"replicas x{world}: every GPU runs the "
+                                       "one-GPU sweep on its own weights, no collective") if world > 1 else "single",
+                       "collective": None if tpw == 1 else (
                            "NCCL all_reduce" if not sweep_hq else
                            "hq_allreduce_sum, NVLS multicast" if any(v[2].value for v in ar_bufs.values())
                            else "hq_allreduce_sum, NVLink peer loads"),

@@ -102,17 +102,23 @@ class QuantLinear:
     """A packed quantized linear layer: tile-order weights + group scales + workspace."""
 
     def __init__(self, W_tile: torch.Tensor, scales: torch.Tensor, K: int, N: int, group: int = 128,
-                 wbits: int = 4, max_m: int = 16):
-        self.W, self.scales, self.K, self.N, self.group = W_tile, scales, K, N, group
+                 wbits: int = 4, max_m: int = 16, bias: torch.Tensor | None = None):
+        self.W, self.scales, self.K, self.N, self.group, self.bias = W_tile, scales, K, N, group, bias
         self.wfmt = HQ_WFMT_TILE_U4 if wbits == 4 else HQ_WFMT_TILE_T2
         self.max_m = max_m
         self.workspace = make_workspace(max_m, N, K, group, self.wfmt, W_tile.device)
+
+    @classmethod
+    def from_q4_k(cls, w_q4k: torch.Tensor, K: int, N: int, max_m: int = 16, stream=None) -> "QuantLinear":
+        """A layer from GGUF Q4_K blocks [N][K/256] on the device (converted once, exactly)."""
+        tile, scales, bias = q4_k_to_tile_u4(w_q4k, K, N, stream=stream)
+        return cls(tile, scales, K, N, group=32, max_m=max_m, bias=bias)
 
     def __call__(self, A: torch.Tensor, out: torch.Tensor | None = None, out_dtype=None, stream=None):
         if A.shape[0] > self.max_m:
             self.max_m = A.shape[0]
             self.workspace = make_workspace(self.max_m, self.N, self.K, self.group, self.wfmt, A.device)
-        return gemm(A, self.W, self.scales, N=self.N, group=self.group, wfmt=self.wfmt, out=out,
+        return gemm(A, self.W, self.scales, N=self.N, group=self.group, wfmt=self.wfmt, bias=self.bias, out=out,
                     out_dtype=out_dtype, workspace=self.workspace, stream=stream)
 
 

@@ -194,3 +194,18 @@ def test_group32_unsupported_combinations_fail_loudly():
     S96 = torch.ones((K // 96 + 1, N), device="cuda:0")
     with pytest.raises(hq.HQError):  # 96 is neither 32 nor a multiple of 64
         hq.gemm(At, W, S96, N=N, group=96)
+
+
+def test_q4_k_quant_linear_and_smallest_shape():
+    """hq.QuantLinear.from_q4_k at the smallest Q4_K layer (one super-block, one strip: K 256,
+    N 16), across the decode / prefill boundary, and M = 0."""
+    K, N = 256, 16
+    blob = o.gen_q4_k_blocks(K, N, seed=5)
+    layer = hq.QuantLinear.from_q4_k(dev_u8(blob), K, N)
+    for M in (1, 16, 17, 64):
+        X = o.round_to((np.random.default_rng(M).standard_normal((M, K)) * 0.5).astype(np.float32), "f16")
+        y = layer(torch.from_numpy(X).to("cuda:0").half(), out_dtype=torch.float32).cpu().numpy()
+        ref = o.q4_k_gemm(X, blob, K, N)
+        assert o.max_rel_err(y, ref) <= (1e-4 if M <= 16 else TOL16["f16"])
+    y0 = layer(torch.empty((0, K), device="cuda:0", dtype=torch.float16))
+    assert tuple(y0.shape) == (0, N)
