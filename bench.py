@@ -548,7 +548,7 @@ def ternary_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
 
 
 def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
-    """GGUF Q4_K at model load: hq_q4_k_to_tile_u4 (GB/s of Q4_K blocks in) and the group-32 GEMM it
+    """GGUF Q4_K at model load: hq_q4_k_to_tile (GB/s of Q4_K blocks in) and the group-32 GEMM it
     feeds (fp16 activations, f32 scale and bias rows per 32 weights) at the 27B shapes, M in {1, 16}
     (decode kernel) and M = 2048 (tcgen05 kernel, TFLOP/s).
     Decode GB/s counts the bytes the kernel must read: codes (K N / 2) plus 8 bytes of scale and bias
@@ -567,14 +567,14 @@ def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
             blob = torch.randint(0, 256, (nblk, 144), dtype=torch.uint8, device=dev, generator=g)
             blob[:, 0:2] = half_bits
             blob[:, 2:4] = half_bits
-            tile = torch.empty(hq.weight_bytes(_lib.HQ_WFMT_TILE_U4, K, N), dtype=torch.uint8, device=dev)
+            tile = torch.empty(hq.weight_bytes(_lib.HQ_WFMT_TILE_U4_K32, K, N), dtype=torch.uint8, device=dev)
             S = torch.empty((K // 32, N), device=dev)
             B = torch.empty((K // 32, N), device=dev)
             copies.append((blob, tile, S, B))
 
         def cv(c):
             blob, tile, S, B = copies[c]
-            st = L.hq_q4_k_to_tile_u4(vp(blob.data_ptr()), vp(tile.data_ptr()), vp(S.data_ptr()), vp(B.data_ptr()),
+            st = L.hq_q4_k_to_tile(vp(blob.data_ptr()), vp(tile.data_ptr()), vp(S.data_ptr()), vp(B.data_ptr()),
                                       K, N, vp(stream.cuda_stream))
             if st != 0:
                 raise RuntimeError(L.hq_last_error_string().decode())
@@ -585,12 +585,12 @@ def q4_k_sweep(torch, L, _lib, hq, dev, stream, peaks, args):
         for M in (1, 16, 2048):
             A = torch.randn((M, K), device=dev, generator=g).half()
             C = torch.empty((M, N), device=dev, dtype=torch.float16)
-            nb = int(L.hq_gemm_workspace_size(M, N, K, 32, _lib.HQ_WFMT_TILE_U4))
+            nb = int(L.hq_gemm_workspace_size(M, N, K, 32, _lib.HQ_WFMT_TILE_U4_K32))
             ws = torch.zeros(max(nb, 16), dtype=torch.uint8, device=dev)
 
             def fn(c):
                 t, s, b = copies[c]
-                st = L.hq_gemm(vp(A.data_ptr()), _lib.HQ_F16, vp(t.data_ptr()), _lib.HQ_WFMT_TILE_U4, vp(s.data_ptr()),
+                st = L.hq_gemm(vp(A.data_ptr()), _lib.HQ_F16, vp(t.data_ptr()), _lib.HQ_WFMT_TILE_U4_K32, vp(s.data_ptr()),
                                _lib.HQ_F32, vp(b.data_ptr()), vp(C.data_ptr()), _lib.HQ_F16, M, N, K, 32,
                                vp(ws.data_ptr()), ws.numel(), vp(stream.cuda_stream))
                 if st != 0:

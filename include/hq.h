@@ -25,12 +25,10 @@
  *   - Shapes: N % 16 == 0, K % 64 == 0, group == 32 or group % 64 == 0,
  *     K % group == 0 (the reference needs K % 512 == 0 and group % 32 == 0:
  *     marlin_gemm.cu:156-159, so every reference shape with group 32 or a
- *     multiple of 64 is accepted).  Group 32 takes int4 weights with f32
- *     scales and runs on the split-K decode kernel for every M (16 rows per
- *     launch): each 64-k block carries two scale (and bias) rows and every
- *     MMA step runs once per 32-k half.  27B shapes at M = 1 with a bias
- *     (the Q4_K form) take 1.2-2.1x the time of a group-128 fp16 layer, for
- *     1.47x the bytes.
+ *     multiple of 64 is accepted).  Group 32 takes int4 weights in
+ *     HQ_WFMT_TILE_U4_K32 (or a reference layout, re-tiled into it) with f32
+ *     scales: M <= 16 runs on the split-K decode kernel (two scale and bias
+ *     rows per 64-k block), larger M on the tcgen05 kernel.
  */
 #ifndef HQ_H
 #define HQ_H
@@ -81,7 +79,12 @@ typedef enum hq_wfmt {
     HQ_WFMT_TILE_T2 = 4,
     /* [N][K/256] blocks of 56 bytes {fp16 d; u8 packed[52]; u16 pad}
      * (native_decoder.cu:32-36). */
-    HQ_WFMT_TQ1_0 = 5
+    HQ_WFMT_TQ1_0 = 5,
+    /* TILE_U4 for scale groups of 32 k: lane t's two words per column hold
+     * k 8t..8t+7 and 32+8t..32+8t+7 of each 64-k block, so every MMA step stays
+     * inside one scale group.  hq_gemm takes group 32 only in this layout (or
+     * from LINEAR_U4 / MARLIN_QUAD, re-tiled into it). */
+    HQ_WFMT_TILE_U4_K32 = 6
 } hq_wfmt;
 
 /* Library version string, e.g. "hq 0.1.0 sm_100a". */
@@ -189,9 +192,9 @@ HQ_API hq_status hq_gemm_noalloc(const void* A, hq_dtype a_dtype,
 /*
  * Weight repack between formats, bit-exact in both directions.
  * Supported (src -> dst): LINEAR_U4 -> MARLIN_QUAD (the reference repack,
- * marlin_gemm.cu:432-467), MARLIN_QUAD -> LINEAR_U4, LINEAR_U4 -> TILE_U4,
- * MARLIN_QUAD -> TILE_U4, TILE_U4 -> LINEAR_U4, LINEAR_T2 -> TILE_T2,
- * TILE_T2 -> LINEAR_T2.
+ * marlin_gemm.cu:432-467), MARLIN_QUAD -> LINEAR_U4, LINEAR_U4 -> TILE_U4
+ * and TILE_U4_K32, MARLIN_QUAD -> TILE_U4 and TILE_U4_K32, TILE_U4 and
+ * TILE_U4_K32 -> LINEAR_U4, LINEAR_T2 -> TILE_T2, TILE_T2 -> LINEAR_T2.
  * hq_repack_host takes host pointers and runs synchronously on host threads
  * (replaces MarlinGemmEngine::repack_q4k_to_marlin, marlin_gemm.hpp:78-83);
  * hq_repack_device takes device pointers and runs on `stream`.
@@ -225,19 +228,19 @@ HQ_API hq_status hq_tq1_0_to_tile_t2(const void* w_tq1, void* tile_t2, void* sca
 /*
  * Model-load conversion of GGUF Q4_K weights (type 12: 256 weights per 144-byte
  * block, gguf_parser.hpp:44,130; laid out [N][K/256] as the native decoder maps
- * GGUF tensors, native_decoder.cu:849-918) into TILE_U4 codes plus f32 group-32
- * scales and biases [K/32][N].  The block fields follow llama.cpp's block_q4_K:
- * fp16 d and dmin, 6-bit scale sc_i and min m_i per 32 weights, 4-bit codes u.
- * Then hq_gemm(A, a, tile_u4, HQ_WFMT_TILE_U4, scales, HQ_F32, bias, C, c, M, N,
- * K, 32, ...) computes with w = u * (d sc_i) - dmin m_i, llama.cpp's
- * dequantize_row_q4_K; scale and bias are exact in f32.
+ * GGUF tensors, native_decoder.cu:849-918) into TILE_U4_K32 codes plus f32
+ * group-32 scales and biases [K/32][N].  The block fields follow llama.cpp's
+ * block_q4_K: fp16 d and dmin, 6-bit scale sc_i and min m_i per 32 weights,
+ * 4-bit codes u.  Then hq_gemm(A, a, tile, HQ_WFMT_TILE_U4_K32, scales, HQ_F32,
+ * bias, C, c, M, N, K, 32, ...) computes with w = u * (d sc_i) - dmin m_i,
+ * llama.cpp's dequantize_row_q4_K; scale and bias are exact in f32.
  * K % 256 == 0, N % 16 == 0; w_q4k 8-byte aligned, the outputs 4-byte aligned.
  * The _host form runs on host threads (nthreads <= 0: all) with host pointers.
  */
-HQ_API hq_status hq_q4_k_to_tile_u4(const void* w_q4k, void* tile_u4, float* scales, float* bias,
-                                    int K, int N, hq_stream_t stream);
-HQ_API hq_status hq_q4_k_to_tile_u4_host(const void* w_q4k, void* tile_u4, float* scales, float* bias,
-                                         int K, int N, int nthreads);
+HQ_API hq_status hq_q4_k_to_tile(const void* w_q4k, void* tile, float* scales, float* bias,
+                                 int K, int N, hq_stream_t stream);
+HQ_API hq_status hq_q4_k_to_tile_host(const void* w_q4k, void* tile, float* scales, float* bias,
+                                      int K, int N, int nthreads);
 
 /*
  * W8A8 GEMM, the reference engine's third precision: activations quantized per

@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_PKG, "libhq.so")
 HQ_OK, HQ_ERR_INVALID_ARG, HQ_ERR_UNSUPPORTED_SHAPE, HQ_ERR_WORKSPACE_TOO_SMALL, HQ_ERR_CUDA, \
     HQ_ERR_TIMEOUT, HQ_ERR_MISALIGNED, HQ_ERR_UNSUPPORTED_DEVICE = range(8)
 HQ_F32, HQ_F16, HQ_BF16 = 0, 1, 2
-HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD, HQ_WFMT_TILE_U4, HQ_WFMT_LINEAR_T2, HQ_WFMT_TILE_T2, HQ_WFMT_TQ1_0 = range(6)
+(HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD, HQ_WFMT_TILE_U4, HQ_WFMT_LINEAR_T2, HQ_WFMT_TILE_T2, HQ_WFMT_TQ1_0,
+ HQ_WFMT_TILE_U4_K32) = range(7)
 HQ_NOALLOC_SCRATCH_BYTES = 64 << 20  # scratch array of hq_gemm_noalloc
 HQ_GGML_F32, HQ_GGML_Q8_0, HQ_GGML_BF16, HQ_GGML_TQ1_0, HQ_GGML_TQ1_0_ALT = 0, 8, 30, 34, 143
 
@@ -36,8 +37,8 @@ SIGNATURES = {
     "hq_repack_device": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "hq_tq1_0_gemv": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "hq_tq1_0_to_tile_t2": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
-    "hq_q4_k_to_tile_u4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
-    "hq_q4_k_to_tile_u4_host": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i]),
+    "hq_q4_k_to_tile": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "hq_q4_k_to_tile_host": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "hq_w8_gemm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "hq_output_projection": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
     "hq_embedding_lookup": (_i, [_vp, _i, _i, _vp, _i, _i, _vp]),

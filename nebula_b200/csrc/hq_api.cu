@@ -150,13 +150,14 @@ int fmt_wbits(hq_wfmt f) {
     switch (f) {
         case HQ_WFMT_LINEAR_U4:
         case HQ_WFMT_MARLIN_QUAD:
-        case HQ_WFMT_TILE_U4: return 4;
+        case HQ_WFMT_TILE_U4:
+        case HQ_WFMT_TILE_U4_K32: return 4;
         case HQ_WFMT_LINEAR_T2:
         case HQ_WFMT_TILE_T2: return 2;
         default: return 0;
     }
 }
-bool fmt_is_tile(hq_wfmt f) { return f == HQ_WFMT_TILE_U4 || f == HQ_WFMT_TILE_T2; }
+bool fmt_is_tile(hq_wfmt f) { return f == HQ_WFMT_TILE_U4 || f == HQ_WFMT_TILE_T2 || f == HQ_WFMT_TILE_U4_K32; }
 
 hq_status check_shape(int M, int N, int K, int group) {
     if (M < 0 || N <= 0 || K <= 0) return fail(HQ_ERR_INVALID_ARG, "negative or zero size M=%d N=%d K=%d", M, N, K);
@@ -200,6 +201,7 @@ HQ_API size_t hq_weight_bytes(hq_wfmt fmt, int K, int N) {
         case HQ_WFMT_MARLIN_QUAD: return (K % 8 || (fmt == HQ_WFMT_MARLIN_QUAD && K % 32)) ? 0 : (size_t)K * N / 2;
         case HQ_WFMT_LINEAR_T2: return K % 16 ? 0 : (size_t)K * N / 4;
         case HQ_WFMT_TILE_U4:
+        case HQ_WFMT_TILE_U4_K32:
         case HQ_WFMT_TILE_T2:
             if (K % 64 || N % 16) return 0;
             return TileGeom(K, N, fmt_wbits(fmt)).bytes();
@@ -239,6 +241,11 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype, const void* Wq, hq_wfm
         (bias && !aligned16(bias)))
         return fail(HQ_ERR_MISALIGNED, "A, Wq, scales, bias, C and workspace must be 16-byte aligned");
     if (bias && wbits != 4) return fail(HQ_ERR_INVALID_ARG, "bias is only defined for int4 weights");
+    if (wfmt == HQ_WFMT_TILE_U4_K32 && group != 32)
+        return fail(HQ_ERR_INVALID_ARG, "HQ_WFMT_TILE_U4_K32 is the group-32 layout (group=%d)", group);
+    if (group == 32 && (wfmt == HQ_WFMT_TILE_U4 || wbits != 4))
+        return fail(HQ_ERR_INVALID_ARG, "group 32 takes int4 weights in HQ_WFMT_TILE_U4_K32 (hq_repack_*, "
+                                        "hq_q4_k_to_tile) or a reference layout");
     int dev = 0;
     if ((st = check_device(&dev)) != HQ_OK) return st;
 
@@ -252,7 +259,7 @@ HQ_API hq_status hq_gemm(const void* A, hq_dtype a_dtype, const void* Wq, hq_wfm
     if (!fmt_is_tile(wfmt)) {
         // Drop-in path: re-tile the reference layout into the workspace first.
         uint8_t* tile = ws;
-        cudaError_t e = launch_linear_to_tile(Wq, wfmt == HQ_WFMT_MARLIN_QUAD, wbits, tile, K, N, s);
+        cudaError_t e = launch_linear_to_tile(Wq, wfmt == HQ_WFMT_MARLIN_QUAD, wbits, tile, K, N, s, group == 32);
         if (e != cudaSuccess) return cuda_fail(e, "re-tile launch");
         W = tile;
         ws += up256(TileGeom(K, N, wbits).bytes());
@@ -317,12 +324,14 @@ HQ_API hq_status hq_repack_host(const void* src, hq_wfmt src_fmt, void* dst, hq_
         return HQ_OK;
     }
     if (K % 64 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "tile order needs K %% 64 == 0 and N %% 16 == 0");
-    if ((src_fmt == HQ_WFMT_LINEAR_U4 || src_fmt == HQ_WFMT_MARLIN_QUAD) && dst_fmt == HQ_WFMT_TILE_U4) {
-        host::linear_to_tile(s, src_fmt == HQ_WFMT_MARLIN_QUAD, 4, d, K, N, nthreads);
+    const bool k32 = dst_fmt == HQ_WFMT_TILE_U4_K32 || src_fmt == HQ_WFMT_TILE_U4_K32;
+    if ((src_fmt == HQ_WFMT_LINEAR_U4 || src_fmt == HQ_WFMT_MARLIN_QUAD) &&
+        (dst_fmt == HQ_WFMT_TILE_U4 || dst_fmt == HQ_WFMT_TILE_U4_K32)) {
+        host::linear_to_tile(s, src_fmt == HQ_WFMT_MARLIN_QUAD, 4, d, K, N, nthreads, k32);
         return HQ_OK;
     }
-    if (src_fmt == HQ_WFMT_TILE_U4 && dst_fmt == HQ_WFMT_LINEAR_U4) {
-        host::tile_to_linear(s, 4, d, K, N, nthreads);
+    if ((src_fmt == HQ_WFMT_TILE_U4 || src_fmt == HQ_WFMT_TILE_U4_K32) && dst_fmt == HQ_WFMT_LINEAR_U4) {
+        host::tile_to_linear(s, 4, d, K, N, nthreads, k32);
         return HQ_OK;
     }
     if (src_fmt == HQ_WFMT_LINEAR_T2 && dst_fmt == HQ_WFMT_TILE_T2) {
@@ -355,10 +364,13 @@ HQ_API hq_status hq_repack_device(const void* src, hq_wfmt src_fmt, void* dst, h
         e = launch_linear_to_quad(sp, dp, K, N, true, s);
     } else {
         if (K % 64 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "tile order needs K %% 64 == 0 and N %% 16 == 0");
-        if ((src_fmt == HQ_WFMT_LINEAR_U4 || src_fmt == HQ_WFMT_MARLIN_QUAD) && dst_fmt == HQ_WFMT_TILE_U4)
-            e = launch_linear_to_tile(src, src_fmt == HQ_WFMT_MARLIN_QUAD, 4, static_cast<uint8_t*>(dst), K, N, s);
-        else if (src_fmt == HQ_WFMT_TILE_U4 && dst_fmt == HQ_WFMT_LINEAR_U4)
-            e = launch_tile_to_linear(static_cast<const uint8_t*>(src), 4, dp, K, N, s);
+        const bool k32 = dst_fmt == HQ_WFMT_TILE_U4_K32 || src_fmt == HQ_WFMT_TILE_U4_K32;
+        if ((src_fmt == HQ_WFMT_LINEAR_U4 || src_fmt == HQ_WFMT_MARLIN_QUAD) &&
+            (dst_fmt == HQ_WFMT_TILE_U4 || dst_fmt == HQ_WFMT_TILE_U4_K32))
+            e = launch_linear_to_tile(src, src_fmt == HQ_WFMT_MARLIN_QUAD, 4, static_cast<uint8_t*>(dst), K, N, s,
+                                      k32);
+        else if ((src_fmt == HQ_WFMT_TILE_U4 || src_fmt == HQ_WFMT_TILE_U4_K32) && dst_fmt == HQ_WFMT_LINEAR_U4)
+            e = launch_tile_to_linear(static_cast<const uint8_t*>(src), 4, dp, K, N, s, k32);
         else if (src_fmt == HQ_WFMT_LINEAR_T2 && dst_fmt == HQ_WFMT_TILE_T2)
             e = launch_linear_to_tile(src, false, 2, static_cast<uint8_t*>(dst), K, N, s);
         else if (src_fmt == HQ_WFMT_TILE_T2 && dst_fmt == HQ_WFMT_LINEAR_T2)
@@ -369,7 +381,7 @@ HQ_API hq_status hq_repack_device(const void* src, hq_wfmt src_fmt, void* dst, h
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "repack launch");
 }
 
-HQ_API hq_status hq_q4_k_to_tile_u4(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
+HQ_API hq_status hq_q4_k_to_tile(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
                                     hq_stream_t stream) {
     if (!w_q4k || !tile_u4 || !scales || !bias) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
     if (K <= 0 || N <= 0 || K % 256 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "need K %% 256 == 0, N %% 16 == 0");
@@ -383,7 +395,7 @@ HQ_API hq_status hq_q4_k_to_tile_u4(const void* w_q4k, void* tile_u4, float* sca
     return e == cudaSuccess ? HQ_OK : cuda_fail(e, "Q4_K conversion launch");
 }
 
-HQ_API hq_status hq_q4_k_to_tile_u4_host(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
+HQ_API hq_status hq_q4_k_to_tile_host(const void* w_q4k, void* tile_u4, float* scales, float* bias, int K, int N,
                                          int nthreads) {
     if (!w_q4k || !tile_u4 || !scales || !bias) return fail(HQ_ERR_INVALID_ARG, "null pointer argument");
     if (K <= 0 || N <= 0 || K % 256 || N % 16) return fail(HQ_ERR_UNSUPPORTED_SHAPE, "need K %% 256 == 0, N %% 16 == 0");

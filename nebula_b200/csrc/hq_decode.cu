@@ -96,6 +96,17 @@ struct XFrag {
         a = *reinterpret_cast<const uint4*>(row + (((2 * t) ^ (r & 7)) << 4));
         b = *reinterpret_cast<const uint4*>(row + (((2 * t + 1) ^ (r & 7)) << 4));
     }
+    // TILE_U4_K32 order: lane t takes chunks t (k 8t..) and t + 4 (k 32 + 8t..).  Odd
+    // rows read the upper chunk first, so the 8 lanes of each quarter warp (rows
+    // 2i, 2i + 1) hit 8 different chunk slots on either load.
+    __device__ __forceinline__ void load_k32(const uint8_t* tile, int r, int t) {
+        const uint8_t* row = tile + r * 128;
+        const bool odd = r & 1;
+        const uint4 p = *reinterpret_cast<const uint4*>(row + (((odd ? t + 4 : t) ^ (r & 7)) << 4));
+        const uint4 q = *reinterpret_cast<const uint4*>(row + (((odd ? t : t + 4) ^ (r & 7)) << 4));
+        a = odd ? q : p;
+        b = odd ? p : q;
+    }
     __device__ __forceinline__ uint32_t b0(int step) const {
         return step == 0 ? a.x : step == 1 ? a.z : step == 2 ? b.x : b.z;
     }
@@ -108,11 +119,13 @@ struct XFrag {
 // two MMAs per step keep the product accurate to ~2^-22 relative.
 struct XFragF32 {
     uint32_t hi[8], lo[8];
-    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t) {
-        const uint8_t* sp = tile + r * (kBlockK * 4 + 16) + 16 * t * 4;
+    // k32: TILE_U4_K32 order, floats 8t.. (steps 0, 1) and 32 + 8t.. (steps 2, 3).
+    __device__ __forceinline__ void load(const uint8_t* tile, int r, int t, bool k32 = false) {
+        const uint8_t* row = tile + r * (kBlockK * 4 + 16);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            uint4 q = *reinterpret_cast<const uint4*>(sp + 16 * i);
+            const uint8_t* sp = k32 ? row + 32 * t + 128 * (i >> 1) + 16 * (i & 1) : row + 64 * t + 16 * i;
+            uint4 q = *reinterpret_cast<const uint4*>(sp);
             float4 v = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z),
                                    __uint_as_float(q.w));
             __half2 h0 = __floats2half2_rn(v.x, v.y);
@@ -345,14 +358,9 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
         const int g = lane >> 2, t = lane & 3;
         using XF = typename std::conditional<kSplit, XFragF32, XFrag<AT>>::type;
         const uint32_t kOnes = 0x3C003C00u;  // fp16 (1, 1) for the bias row sums
-        // Group-32 scales: lane t's activation fragments hold k [16t, 16t + 16)
-        // of a block (tile order), so lanes t < 2 carry scale group 2kb and
-        // lanes t >= 2 group 2kb + 1.  Each MMA runs once per group with the
-        // other group's lanes zeroed, keeping the two sums apart.
-        auto half_mask = [&](int h) -> uint32_t {
-            if constexpr (kG32) return ((t >> 1) == h) ? 0xffffffffu : 0u;
-            else return 0xffffffffu;
-        };
+        // Group 32 (TILE_U4_K32 weights): MMA steps 0, 1 of a block cover its
+        // k [0, 32) (scale group 2kb), steps 2, 3 its k [32, 64) (group 2kb + 1).
+        constexpr int kStepsPerRow = kG32 ? 2 : 4;  // MMA steps per scale row
         // After a timed-out wait the warp stops waiting but keeps the same
         // control flow (results are garbage, the error word is set): every
         // thread still reaches the barriers below, so nothing hangs.
@@ -377,7 +385,11 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                 if (u >= nu) continue;
                 const uint8_t* tile = stage + L::kX + u * L::kXUnit;
 #pragma unroll
-                for (int m = 0; m < MT; ++m) xf[u][m].load(tile, 8 * m + g, t);
+                for (int m = 0; m < MT; ++m) {
+                    if constexpr (!kG32) xf[u][m].load(tile, 8 * m + g, t);
+                    else if constexpr (kSplit) xf[u][m].load(tile, 8 * m + g, t, true);
+                    else xf[u][m].load_k32(tile, 8 * m + g, t);
+                }
                 // Rows >= M are zero (TMA fill) or stale (padded copies); either way
                 // they only feed MMA columns (tokens) that are never stored.
 #pragma unroll
@@ -406,17 +418,16 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                     const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
 #pragma unroll
                     for (int h = 0; h < L::kSRows; ++h) {
-                        const uint32_t mk = half_mask(h);
 #pragma unroll
                         for (int m = 0; m < MT; ++m) {
                             float x4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                            for (int s = 0; s < 4; ++s) {
+                            for (int s = kStepsPerRow * h; s < kStepsPerRow * (h + 1); ++s) {
                                 if constexpr (kSplit) {
-                                    mma_16816<false>(x4, ones, xf[u][m].hi[2 * s] & mk, xf[u][m].hi[2 * s + 1] & mk);
-                                    mma_16816<false>(x4, ones, xf[u][m].lo[2 * s] & mk, xf[u][m].lo[2 * s + 1] & mk);
+                                    mma_16816<false>(x4, ones, xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                    mma_16816<false>(x4, ones, xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
                                 } else {
-                                    mma_16816<kBF16>(x4, ones, xf[u][m].b0(s) & mk, xf[u][m].b1(s) & mk);
+                                    mma_16816<kBF16>(x4, ones, xf[u][m].b0(s), xf[u][m].b1(s));
                                 }
                             }
                             xs[u][h][m][0] = x4[0];
@@ -441,21 +452,18 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const
                         wf.build(wv);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
-                            const uint32_t mk = half_mask(h);
                             float tacc[MT][4];
 #pragma unroll
                             for (int m = 0; m < MT; ++m) {
 #pragma unroll
                                 for (int i = 0; i < 4; ++i) tacc[m][i] = 0.f;
 #pragma unroll
-                                for (int s = 0; s < 4; ++s) {
+                                for (int s = 2 * h; s < 2 * h + 2; ++s) {
                                     if constexpr (kSplit) {
-                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].hi[2 * s] & mk,
-                                                         xf[u][m].hi[2 * s + 1] & mk);
-                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].lo[2 * s] & mk,
-                                                         xf[u][m].lo[2 * s + 1] & mk);
+                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].hi[2 * s], xf[u][m].hi[2 * s + 1]);
+                                        mma_16816<false>(tacc[m], wf.r[s], xf[u][m].lo[2 * s], xf[u][m].lo[2 * s + 1]);
                                     } else {
-                                        mma_16816<kBF16>(tacc[m], wf.r[s], xf[u][m].b0(s) & mk, xf[u][m].b1(s) & mk);
+                                        mma_16816<kBF16>(tacc[m], wf.r[s], xf[u][m].b0(s), xf[u][m].b1(s));
                                     }
                                 }
                             }

@@ -63,17 +63,20 @@ bool prefill_supported(const GemmArgs& a);
 cudaError_t launch_prefill(const GemmArgs& a);
 
 // Repack kernels (device).
+// k32: the TILE_U4_K32 order (int4, group 32).
 cudaError_t launch_linear_to_tile(const void* src, bool src_is_quad, int wbits, uint8_t* dst, int K, int N,
-                                  cudaStream_t s);
-cudaError_t launch_tile_to_linear(const uint8_t* src, int wbits, uint32_t* dst, int K, int N, cudaStream_t s);
+                                  cudaStream_t s, bool k32 = false);
+cudaError_t launch_tile_to_linear(const uint8_t* src, int wbits, uint32_t* dst, int K, int N, cudaStream_t s,
+                                  bool k32 = false);
 cudaError_t launch_linear_to_quad(const uint32_t* src, uint32_t* dst, int K, int N, bool inverse, cudaStream_t s);
-// GGUF Q4_K [N][K/256] blocks -> TILE_U4 codes + f32 group-32 scales and biases [K/32][N].
+// GGUF Q4_K [N][K/256] blocks -> TILE_U4_K32 codes + f32 group-32 scales and biases [K/32][N].
 cudaError_t launch_q4k_to_tile(const uint8_t* w, uint8_t* tile, float* scales, float* bias, int K, int N,
                                cudaStream_t s);
 
 namespace host {
-void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, int K, int N, int nthreads);
-void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N, int nthreads);
+void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, int K, int N, int nthreads,
+                    bool k32 = false);
+void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N, int nthreads, bool k32 = false);
 void linear_quad(const uint32_t* src, uint32_t* dst, int K, int N, bool inverse, int nthreads);
 void q4k_to_tile(const uint8_t* w, uint32_t* tile, float* scales, float* bias, int K, int N, int nthreads);
 }  // namespace host

@@ -25,6 +25,12 @@
 // nibble of each byte (nibbles 0/4 and 2/6) and (e4,e5), (e6,e7) in the high
 // nibble (1/5 and 3/7): one MMA step draws all its pairs from one of the two
 // nibble classes, so a class is expanded with a single mask per pair.
+//
+// TILE_U4_K32, the layout for scale groups of 32 k: the same chunks, words and
+// nibble order, but word j of lane t holds k = 64kb + 8t + 32*(j&1) + e.  The
+// MMA steps built from word j = 0 (steps 0, 1) then lie in k [0, 32) of the
+// block and those from j = 1 (steps 2, 3) in [32, 64): each step belongs to
+// one scale group.  The activation fragments relabel k the same way.
 #pragma once
 
 #include <stddef.h>
@@ -105,12 +111,12 @@ HQ_HD uint32_t t2_tile_to_linear(uint32_t w) {
 
 // For tile word (s, kb, lane, j): the output column and the linear-format
 // word row (kw) it mirrors.  int4 linear words hold 8 k (kw = k/8), ternary
-// linear words hold 16 k (kw = k/16).
-HQ_HD void tile_word_source(int wbits, int s, int kb, int lane, int j, int* col, int* kw) {
+// linear words hold 16 k (kw = k/16).  k32: the TILE_U4_K32 order.
+HQ_HD void tile_word_source(int wbits, int s, int kb, int lane, int j, int* col, int* kw, bool k32 = false) {
     int g = lane >> 2, t = lane & 3;
     if (wbits == 4) {
         *col = s * kStripCols + g + 8 * (j >> 1);
-        *kw = (kb * kBlockK + 16 * t + 8 * (j & 1)) / 8;
+        *kw = k32 ? (kb * kBlockK + 8 * t + 32 * (j & 1)) / 8 : (kb * kBlockK + 16 * t + 8 * (j & 1)) / 8;
     } else {
         *col = s * kStripCols + g + 8 * j;
         *kw = (kb * kBlockK + 16 * t) / 16;

@@ -299,10 +299,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(const __grid_co
                     uint32_t r[8];
                     if constexpr (kF32S) {
                         // k 16t .. 16t+15 lie in the block's 32-k half t / 2
+                        // the two words of k 16t .. 16t+15: TILE_U4 has them as lane t's
+                        // pair; TILE_U4_K32 (group 32) as the first (t < 2) or second word
+                        // of lanes 2(t % 2) and 2(t % 2) + 1
+                        const bool k32 = p.group == 32;
+                        const uint32_t w0 = k32 ? cw[4 * (t & 1) + (t >> 1)] : cw[2 * t];
+                        const uint32_t w1 = k32 ? cw[4 * (t & 1) + 2 + (t >> 1)] : cw[2 * t + 1];
                         const float s = sv[t >> 1], b = bv[t >> 1];
                         uint32_t lo[4], hi[4];
-                        affine_word<kBF16>(cw[2 * t], s, b, lo);
-                        affine_word<kBF16>(cw[2 * t + 1], s, b, hi);
+                        affine_word<kBF16>(w0, s, b, lo);
+                        affine_word<kBF16>(w1, s, b, hi);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             r[e] = lo[e];

@@ -23,7 +23,7 @@ __device__ __forceinline__ uint32_t load_linear_word(const uint32_t* src, bool q
 }
 
 __global__ void linear_to_tile_kernel(const uint32_t* __restrict__ src, bool quad, int wbits,
-                                      uint32_t* __restrict__ dst, int K, int N) {
+                                      uint32_t* __restrict__ dst, int K, int N, bool k32) {
     const TileGeom geo(K, N, wbits);
     const int words_per_lane = wbits == 4 ? 4 : 2;
     const size_t total = geo.bytes() / 4;
@@ -40,14 +40,14 @@ __global__ void linear_to_tile_kernel(const uint32_t* __restrict__ src, bool qua
         const int kb = (int)(rem / w), sl = (int)(rem % w);
         const int s = sg * kGroupStrips + sl;
         int col, kw;
-        tile_word_source(wbits, s, kb, lane, j, &col, &kw);
+        tile_word_source(wbits, s, kb, lane, j, &col, &kw, k32);
         const uint32_t v = load_linear_word(src, quad, kw, col, N);
         dst[i] = wbits == 4 ? u4_linear_to_tile(v) : t2_linear_to_tile(v);
     }
 }
 
 __global__ void tile_to_linear_kernel(const uint32_t* __restrict__ src, int wbits, uint32_t* __restrict__ dst,
-                                      int K, int N) {
+                                      int K, int N, bool k32) {
     const TileGeom geo(K, N, wbits);
     const int words_per_lane = wbits == 4 ? 4 : 2;
     const size_t total = geo.bytes() / 4;
@@ -62,7 +62,7 @@ __global__ void tile_to_linear_kernel(const uint32_t* __restrict__ src, int wbit
         const int kb = (int)(rem / w), sl = (int)(rem % w);
         const int s = sg * kGroupStrips + sl;
         int col, kw;
-        tile_word_source(wbits, s, kb, lane, j, &col, &kw);
+        tile_word_source(wbits, s, kb, lane, j, &col, &kw, k32);
         const uint32_t v = __ldg(src + i);
         dst[(size_t)kw * N + col] = wbits == 4 ? u4_tile_to_linear(v) : t2_tile_to_linear(v);
     }
@@ -166,7 +166,7 @@ HQ_HD void q4k_scale_bias(const uint8_t* w, int K, int g, int n, float* scale, f
     *bias = -(dmin * (float)m);
 }
 
-// Tile word i (storage order) -> its column and first k.
+// Tile word i (storage order, TILE_U4_K32) -> its column and first k.
 HQ_HD void tile_word_coords(const TileGeom& geo, size_t i, int* col, int* k0) {
     const size_t chunk = i / 128;  // int4: 32 lanes x 4 words per chunk
     const int within = (int)(i % 128);
@@ -177,7 +177,7 @@ HQ_HD void tile_word_coords(const TileGeom& geo, size_t i, int* col, int* k0) {
     const int w = geo.width(sg);
     const int kb = (int)(rem / w), sl = (int)(rem % w);
     int kw;
-    tile_word_source(4, sg * kGroupStrips + sl, kb, lane, j, col, &kw);
+    tile_word_source(4, sg * kGroupStrips + sl, kb, lane, j, col, &kw, true);
     *k0 = kw * 8;
 }
 
@@ -208,18 +208,19 @@ cudaError_t launch_q4k_to_tile(const uint8_t* w, uint8_t* tile, float* scales, f
 }
 
 cudaError_t launch_linear_to_tile(const void* src, bool src_is_quad, int wbits, uint8_t* dst, int K, int N,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, bool k32) {
     const TileGeom geo(K, N, wbits);
     linear_to_tile_kernel<<<grid_for(geo.bytes() / 4), 256, 0, s>>>(reinterpret_cast<const uint32_t*>(src),
                                                                     src_is_quad, wbits,
-                                                                    reinterpret_cast<uint32_t*>(dst), K, N);
+                                                                    reinterpret_cast<uint32_t*>(dst), K, N, k32);
     return cudaGetLastError();
 }
 
-cudaError_t launch_tile_to_linear(const uint8_t* src, int wbits, uint32_t* dst, int K, int N, cudaStream_t s) {
+cudaError_t launch_tile_to_linear(const uint8_t* src, int wbits, uint32_t* dst, int K, int N, cudaStream_t s,
+                                  bool k32) {
     const TileGeom geo(K, N, wbits);
     tile_to_linear_kernel<<<grid_for(geo.bytes() / 4), 256, 0, s>>>(reinterpret_cast<const uint32_t*>(src), wbits,
-                                                                    dst, K, N);
+                                                                    dst, K, N, k32);
     return cudaGetLastError();
 }
 
@@ -249,7 +250,7 @@ void parallel_for(size_t n, int nthreads, F&& f) {
     for (auto& x : th) x.join();
 }
 
-void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, int K, int N, int nthreads) {
+void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, int K, int N, int nthreads, bool k32) {
     const TileGeom geo(K, N, wbits);
     const int wpl = wbits == 4 ? 4 : 2;
     const size_t total = geo.bytes() / 4;
@@ -264,14 +265,14 @@ void linear_to_tile(const uint32_t* src, bool quad, int wbits, uint32_t* dst, in
             const int w = geo.width(sg);
             const int kb = (int)(rem / w), sl = (int)(rem % w);
             int col, kw;
-            tile_word_source(wbits, sg * kGroupStrips + sl, kb, lane, j, &col, &kw);
+            tile_word_source(wbits, sg * kGroupStrips + sl, kb, lane, j, &col, &kw, k32);
             const uint32_t v = quad ? src[((size_t)(kw >> 2) * N + col) * 4 + (kw & 3)] : src[(size_t)kw * N + col];
             dst[i] = wbits == 4 ? u4_linear_to_tile(v) : t2_linear_to_tile(v);
         }
     });
 }
 
-void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N, int nthreads) {
+void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N, int nthreads, bool k32) {
     const TileGeom geo(K, N, wbits);
     const int wpl = wbits == 4 ? 4 : 2;
     const size_t total = geo.bytes() / 4;
@@ -286,7 +287,7 @@ void tile_to_linear(const uint32_t* src, int wbits, uint32_t* dst, int K, int N,
             const int w = geo.width(sg);
             const int kb = (int)(rem / w), sl = (int)(rem % w);
             int col, kw;
-            tile_word_source(wbits, sg * kGroupStrips + sl, kb, lane, j, &col, &kw);
+            tile_word_source(wbits, sg * kGroupStrips + sl, kb, lane, j, &col, &kw, k32);
             const uint32_t v = src[i];
             dst[(size_t)kw * N + col] = wbits == 4 ? u4_tile_to_linear(v) : t2_tile_to_linear(v);
         }

@@ -19,13 +19,13 @@ import torch
 
 from . import _lib
 from ._lib import (HQ_BF16, HQ_F16, HQ_F32, HQ_WFMT_LINEAR_T2, HQ_WFMT_LINEAR_U4, HQ_WFMT_MARLIN_QUAD,
-                   HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TQ1_0, HQError, check, lib)
+                   HQ_WFMT_TILE_T2, HQ_WFMT_TILE_U4, HQ_WFMT_TILE_U4_K32, HQ_WFMT_TQ1_0, HQError, check, lib)
 
 __all__ = ["HQError", "weight_bytes", "repack_host", "repack", "make_workspace", "gemm", "QuantLinear",
-           "tq1_0_gemv", "tq1_0_to_tile_t2", "q4_k_to_tile_u4", "q4_k_to_tile_u4_host", "output_projection", "embedding_lookup", "w8_gemm", "check_device_error",
+           "tq1_0_gemv", "tq1_0_to_tile_t2", "q4_k_to_tile", "q4_k_to_tile_host", "output_projection", "embedding_lookup", "w8_gemm", "check_device_error",
            "MarlinGemmEngine",
            "HQ_WFMT_LINEAR_U4", "HQ_WFMT_MARLIN_QUAD", "HQ_WFMT_TILE_U4", "HQ_WFMT_LINEAR_T2",
-           "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0"]
+           "HQ_WFMT_TILE_T2", "HQ_WFMT_TQ1_0", "HQ_WFMT_TILE_U4_K32"]
 
 _DT = {torch.float32: HQ_F32, torch.float16: HQ_F16, torch.bfloat16: HQ_BF16}
 
@@ -84,10 +84,13 @@ def make_workspace(M: int, N: int, K: int, group: int, wfmt: int, device) -> tor
 
 
 def gemm(A: torch.Tensor, W: torch.Tensor, scales: torch.Tensor, *, N: int, group: int = 128,
-         wfmt: int = HQ_WFMT_TILE_U4, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         wfmt: int | None = None, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
          out_dtype: torch.dtype | None = None, workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """C = A @ dequant(W) through hq_gemm.  A: [M, K] device tensor."""
+    """C = A @ dequant(W) through hq_gemm.  A: [M, K] device tensor.  wfmt defaults to the tile
+    order of the group: TILE_U4_K32 for group 32, TILE_U4 otherwise."""
     M, K = A.shape
+    if wfmt is None:
+        wfmt = HQ_WFMT_TILE_U4_K32 if group == 32 else HQ_WFMT_TILE_U4
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
     if workspace is None:
@@ -104,14 +107,14 @@ class QuantLinear:
     def __init__(self, W_tile: torch.Tensor, scales: torch.Tensor, K: int, N: int, group: int = 128,
                  wbits: int = 4, max_m: int = 16, bias: torch.Tensor | None = None):
         self.W, self.scales, self.K, self.N, self.group, self.bias = W_tile, scales, K, N, group, bias
-        self.wfmt = HQ_WFMT_TILE_U4 if wbits == 4 else HQ_WFMT_TILE_T2
+        self.wfmt = (HQ_WFMT_TILE_U4_K32 if group == 32 else HQ_WFMT_TILE_U4) if wbits == 4 else HQ_WFMT_TILE_T2
         self.max_m = max_m
         self.workspace = make_workspace(max_m, N, K, group, self.wfmt, W_tile.device)
 
     @classmethod
     def from_q4_k(cls, w_q4k: torch.Tensor, K: int, N: int, max_m: int = 16, stream=None) -> "QuantLinear":
         """A layer from GGUF Q4_K blocks [N][K/256] on the device (converted once, exactly)."""
-        tile, scales, bias = q4_k_to_tile_u4(w_q4k, K, N, stream=stream)
+        tile, scales, bias = q4_k_to_tile(w_q4k, K, N, stream=stream)
         return cls(tile, scales, K, N, group=32, max_m=max_m, bias=bias)
 
     def __call__(self, A: torch.Tensor, out: torch.Tensor | None = None, out_dtype=None, stream=None):
@@ -172,24 +175,24 @@ def tq1_0_to_tile_t2(w: torch.Tensor, K: int, N: int, stream=None):
     return tile, scales
 
 
-def q4_k_to_tile_u4(w: torch.Tensor, K: int, N: int, stream=None):
-    """GGUF Q4_K blocks [N][K/256] (uint8, device) -> (TILE_U4 codes, f32 scales [K/32, N],
+def q4_k_to_tile(w: torch.Tensor, K: int, N: int, stream=None):
+    """GGUF Q4_K blocks [N][K/256] (uint8, device) -> (TILE_U4_K32 codes, f32 scales [K/32, N],
     f32 bias [K/32, N]) for gemm(..., bias=bias, group=32)."""
-    tile = torch.empty(weight_bytes(HQ_WFMT_TILE_U4, K, N), dtype=torch.uint8, device=w.device)
+    tile = torch.empty(weight_bytes(HQ_WFMT_TILE_U4_K32, K, N), dtype=torch.uint8, device=w.device)
     scales = torch.empty((K // 32, N), dtype=torch.float32, device=w.device)
     bias = torch.empty((K // 32, N), dtype=torch.float32, device=w.device)
-    check(lib().hq_q4_k_to_tile_u4(_ptr(w), _ptr(tile), _ptr(scales), _ptr(bias), K, N, _stream(stream)))
+    check(lib().hq_q4_k_to_tile(_ptr(w), _ptr(tile), _ptr(scales), _ptr(bias), K, N, _stream(stream)))
     return tile, scales, bias
 
 
-def q4_k_to_tile_u4_host(w: np.ndarray, K: int, N: int, nthreads: int = 0):
-    """Host-thread form of q4_k_to_tile_u4 on numpy arrays."""
+def q4_k_to_tile_host(w: np.ndarray, K: int, N: int, nthreads: int = 0):
+    """Host-thread form of q4_k_to_tile on numpy arrays."""
     src = np.ascontiguousarray(w, dtype=np.uint8)
-    tile = np.empty(weight_bytes(HQ_WFMT_TILE_U4, K, N), np.uint8)
+    tile = np.empty(weight_bytes(HQ_WFMT_TILE_U4_K32, K, N), np.uint8)
     scales = np.empty((K // 32, N), np.float32)
     bias = np.empty((K // 32, N), np.float32)
     vp = ctypes.c_void_p
-    check(lib().hq_q4_k_to_tile_u4_host(src.ctypes.data_as(vp), tile.ctypes.data_as(vp), scales.ctypes.data_as(vp),
+    check(lib().hq_q4_k_to_tile_host(src.ctypes.data_as(vp), tile.ctypes.data_as(vp), scales.ctypes.data_as(vp),
                                         bias.ctypes.data_as(vp), K, N, nthreads))
     return tile, scales, bias
 

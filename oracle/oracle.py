@@ -179,6 +179,26 @@ def unpack_tile(tile: np.ndarray, K: int, N: int, wbits: int) -> np.ndarray:
     return q
 
 
+def _k32_perm(K: int) -> np.ndarray:
+    """Row order that turns TILE_U4 into TILE_U4_K32: tile position 16t + 8j + e of a 64-k
+    block holds k = 8t + 32j + e (hq.h HQ_WFMT_TILE_U4_K32)."""
+    d = np.arange(64)
+    t, j, e = d // 16, (d // 8) % 2, d % 8
+    src = 8 * t + 32 * j + e
+    return (np.arange(K) // 64) * 64 + src[np.arange(K) % 64]
+
+
+def pack_tile_k32(q: np.ndarray) -> np.ndarray:
+    """TILE_U4_K32 bytes of int4 codes q [K][N]: the tile packer on k-permuted rows."""
+    return pack_tile(np.ascontiguousarray(q[_k32_perm(q.shape[0])]), 4)
+
+
+def unpack_tile_k32(tile: np.ndarray, K: int, N: int) -> np.ndarray:
+    q = np.empty((K, N), np.int8)
+    q[_k32_perm(K)] = unpack_tile(tile, K, N, 4)
+    return q
+
+
 def pack_tq1_0(t_nk: np.ndarray, d_bits: np.ndarray) -> np.ndarray:
     N, K = t_nk.shape
     out = np.empty(N * (K // 256) * 56, np.uint8)
@@ -337,9 +357,9 @@ def dequant_q4_k(blob: np.ndarray, K: int, N: int) -> np.ndarray:
 
 
 def q4_k_to_tile(blob: np.ndarray, K: int, N: int):
-    """The oracle's Q4_K -> (TILE_U4 bytes, scale, bias): the tile packer on q = u - 8."""
+    """The oracle's Q4_K -> (TILE_U4_K32 bytes, scale, bias): the packer on q = u - 8."""
     u, scale, bias = unpack_q4_k(blob, K, N)
-    return pack_tile(u.astype(np.int8) - 8, 4), scale, bias
+    return pack_tile_k32(u.astype(np.int8) - 8), scale, bias
 
 
 def q4_k_gemm(X, blob, K, N, nthreads=0):

@@ -26,7 +26,7 @@ def dev_u8(a):
 
 
 def check_conversion(blob, K, N):
-    tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
+    tile, s, b = hq.q4_k_to_tile(dev_u8(blob), K, N)
     torch.cuda.synchronize()
     with np.errstate(invalid="ignore"):
         t_ref, s_ref, b_ref = o.q4_k_to_tile(blob, K, N)
@@ -64,7 +64,7 @@ def test_q4_k_gemm_parity(M, a_dtype):
     K, N = 1024, 272
     blob, X = q4k_case(M, K, N, 100 + M, a_dtype)
     ref = o.q4_k_gemm(X, blob, K, N)
-    tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
+    tile, s, b = hq.q4_k_to_tile(dev_u8(blob), K, N)
     Xt = torch.from_numpy(X).to("cuda:0").to(TDT[a_dtype])
     y32 = hq.gemm(Xt, tile, s, N=N, group=32, bias=b, out_dtype=torch.float32)
     torch.cuda.synchronize()
@@ -96,7 +96,7 @@ def test_q4_k_prefill(M):
     """M > 16: the tcgen05 kernel's f32-scale form (two scale and bias rows per 64-k block)."""
     K, N = 1024, 272
     blob, X = q4k_case(M, K, N, 200 + M, "f16")
-    tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
+    tile, s, b = hq.q4_k_to_tile(dev_u8(blob), K, N)
     Xt = torch.from_numpy(X).to("cuda:0").half()
     y = hq.gemm(Xt, tile, s, N=N, group=32, bias=b, out_dtype=torch.float32).cpu().numpy()
     hq.check_device_error()
@@ -118,7 +118,7 @@ def test_prefill_f32_scales(M, K, N, g, a_dtype, with_bias):
     A, q, _ = o.gen_int4_case(M, K, N, group=g, seed=M + N, a_dtype=a_dtype)
     S = (0.005 + rng.random((K // g, N)) * 0.015).astype(np.float32)
     B = (-8.0 * S + 0.01 * rng.standard_normal(S.shape)).astype(np.float32) if with_bias else None
-    W = dev_u8(o.pack_tile(q, 4))
+    W = dev_u8(o.pack_tile_k32(q) if g == 32 else o.pack_tile(q, 4))
     At = torch.from_numpy(A).to("cuda:0").to(TDT[a_dtype])
     Bt = torch.from_numpy(B).to("cuda:0") if with_bias else None
     y = hq.gemm(At, W, torch.from_numpy(S).to("cuda:0"), N=N, group=g, bias=Bt, out_dtype=torch.float32)
@@ -138,7 +138,7 @@ def test_q4_k_27b_qkv_shape(M):
     blob, X = q4k_case(M, K, N, 7 + M, "f16")
     rows = np.arange(M) if M <= 16 else np.arange(0, M, 61)  # sampled rows at M = 2048
     ref = o.q4_k_gemm(X[rows], blob, K, N)
-    tile, s, b = hq.q4_k_to_tile_u4(dev_u8(blob), K, N)
+    tile, s, b = hq.q4_k_to_tile(dev_u8(blob), K, N)
     y = hq.gemm(torch.from_numpy(X).to("cuda:0").half(), tile, s, N=N, group=32, bias=b,
                 out_dtype=torch.float32).cpu().numpy()
     assert o.max_rel_err(y[rows], ref) <= (1e-4 if M <= 16 else TOL16["f16"])
@@ -151,7 +151,7 @@ def test_group32_symmetric(M, a_dtype):
     K, N = 512, 144
     A, q, S = o.gen_int4_case(M, K, N, group=32, seed=M + 3, a_dtype=a_dtype, s_dtype="f32")
     ref = o.w4_gemm(A, o.pack_linear_u4(q), S, group=32)
-    W = dev_u8(o.pack_tile(q, 4))
+    W = dev_u8(o.pack_tile_k32(q))
     At = torch.from_numpy(A).to("cuda:0").to(TDT[a_dtype])
     St = torch.from_numpy(S).to("cuda:0")
     y = hq.gemm(At, W, St, N=N, group=32, out_dtype=torch.float32).cpu().numpy()
@@ -187,10 +187,15 @@ def test_group32_reference_layouts():
 def test_group32_unsupported_combinations_fail_loudly():
     K, N = 512, 144
     A, q, S = o.gen_int4_case(4, K, N, group=32, seed=1, a_dtype="f16")
-    W = dev_u8(o.pack_tile(q, 4))
+    W = dev_u8(o.pack_tile_k32(q))
     At = torch.from_numpy(A).to("cuda:0").half()
     with pytest.raises(hq.HQError):  # group 32 takes f32 scales only
         hq.gemm(At, W, torch.from_numpy(S).to("cuda:0").half(), N=N, group=32)
+    S32 = torch.from_numpy(S).to("cuda:0")
+    with pytest.raises(hq.HQError):  # group 32 takes the TILE_U4_K32 order, not TILE_U4
+        hq.gemm(At, W, S32, N=N, group=32, wfmt=hq.HQ_WFMT_TILE_U4)
+    with pytest.raises(hq.HQError):  # and TILE_U4_K32 is only for group 32
+        hq.gemm(At, W, torch.ones((K // 64, N), device="cuda:0"), N=N, group=64, wfmt=hq.HQ_WFMT_TILE_U4_K32)
     S96 = torch.ones((K // 96 + 1, N), device="cuda:0")
     with pytest.raises(hq.HQError):  # 96 is neither 32 nor a multiple of 64
         hq.gemm(At, W, S96, N=N, group=96)
@@ -209,3 +214,16 @@ def test_q4_k_quant_linear_and_smallest_shape():
         assert o.max_rel_err(y, ref) <= (1e-4 if M <= 16 else TOL16["f16"])
     y0 = layer(torch.empty((0, K), device="cuda:0", dtype=torch.float16))
     assert tuple(y0.shape) == (0, N)
+
+
+@pytest.mark.parametrize("K,N", [(512, 272), (5120, 7168)])
+def test_device_repack_k32(K, N):
+    """hq_repack_device LINEAR_U4 / MARLIN_QUAD -> TILE_U4_K32 and back, bit for bit."""
+    q = np.random.default_rng(K).integers(-8, 8, size=(K, N), dtype=np.int8)
+    lin = o.pack_linear_u4(q)
+    want = o.pack_tile_k32(q)
+    for fmt, src in ((hq.HQ_WFMT_LINEAR_U4, lin), (hq.HQ_WFMT_MARLIN_QUAD, o.repack_marlin_quad(lin, K, N))):
+        t = hq.repack(dev_u8(src), fmt, hq.HQ_WFMT_TILE_U4_K32, K, N)
+        assert np.array_equal(t.cpu().numpy(), want)
+    back = hq.repack(dev_u8(want), hq.HQ_WFMT_TILE_U4_K32, hq.HQ_WFMT_LINEAR_U4, K, N)
+    assert np.array_equal(back.cpu().numpy().view(np.uint32).reshape(lin.shape), lin)

@@ -33,9 +33,9 @@ def test_oracle_dequant_matches_gguf_fixture(case):
 @pytest.mark.parametrize("case", _cases(), ids=lambda c: c[0])
 @pytest.mark.parametrize("nthreads", [1, 0])
 def test_host_conversion_matches_oracle(case, nthreads):
-    """hq_q4_k_to_tile_u4_host: tile codes, scales and biases identical to the oracle's."""
+    """hq_q4_k_to_tile_host: tile codes, scales and biases identical to the oracle's."""
     _, K, N, blob, _ = case
-    tile, scale, bias = hq.q4_k_to_tile_u4_host(blob, K, N, nthreads)
+    tile, scale, bias = hq.q4_k_to_tile_host(blob, K, N, nthreads)
     with np.errstate(invalid="ignore"):
         t_ref, s_ref, b_ref = o.q4_k_to_tile(blob, K, N)
     assert np.array_equal(tile, t_ref)
@@ -47,13 +47,29 @@ def test_host_conversion_ragged_strip_group():
     """N = 272: the last strip group holds one strip (ragged), K spans several super-blocks."""
     K, N = 768, 272
     blob = o.gen_q4_k_blocks(K, N, seed=11)
-    tile, scale, bias = hq.q4_k_to_tile_u4_host(blob, K, N)
+    tile, scale, bias = hq.q4_k_to_tile_host(blob, K, N)
     t_ref, s_ref, b_ref = o.q4_k_to_tile(blob, K, N)
     assert np.array_equal(tile, t_ref)
     assert np.array_equal(scale, s_ref) and np.array_equal(bias, b_ref)
     # the tile codes decode back to u - 8 of the block codes
     u, _, _ = o.unpack_q4_k(blob, K, N)
-    assert np.array_equal(o.unpack_tile(tile, K, N, 4), u.astype(np.int8) - 8)
+    assert np.array_equal(o.unpack_tile_k32(tile, K, N), u.astype(np.int8) - 8)
+
+
+@pytest.mark.parametrize("src", ["linear", "quad"])
+def test_host_repack_to_k32_layout(src):
+    """hq_repack_host LINEAR_U4 / MARLIN_QUAD -> TILE_U4_K32 equals the oracle's K32 packer, and
+    TILE_U4_K32 -> LINEAR_U4 inverts it bit for bit."""
+    K, N = 512, 272
+    q = np.random.default_rng(3).integers(-8, 8, size=(K, N), dtype=np.int8)
+    lin = o.pack_linear_u4(q)
+    s = lin if src == "linear" else o.repack_marlin_quad(lin, K, N)
+    fmt = hq.HQ_WFMT_LINEAR_U4 if src == "linear" else hq.HQ_WFMT_MARLIN_QUAD
+    t = hq.repack_host(s, fmt, hq.HQ_WFMT_TILE_U4_K32, K, N)
+    assert np.array_equal(t.view(np.uint8).reshape(-1), o.pack_tile_k32(q))
+    back = hq.repack_host(t, hq.HQ_WFMT_TILE_U4_K32, hq.HQ_WFMT_LINEAR_U4, K, N)
+    assert np.array_equal(back.reshape(lin.shape), lin)
+    assert not np.array_equal(o.pack_tile_k32(q), o.pack_tile(q, 4))  # the two orders differ
 
 
 def test_scale_and_bias_exact_in_f32():
@@ -82,4 +98,4 @@ def test_oracle_gemm_matches_dequantised_product():
 def test_host_conversion_rejects_bad_shapes(K, N):
     blob = np.zeros(max(1, N * max(K, 256) // 256 * 144), np.uint8)
     with pytest.raises(hq.HQError):
-        hq.q4_k_to_tile_u4_host(blob, K, N)
+        hq.q4_k_to_tile_host(blob, K, N)
