@@ -805,6 +805,21 @@ def run_case(args):
         hq.check_device_error()
         print(json.dumps({"case": args.case, "checksum": float(y.abs().sum())}))
         return 0
+    if f[0] == "q4k":  # q4k,K,N,M: GGUF Q4_K blocks (d = dmin = 0.002) converted once, then the group-32 GEMM
+        K, N, M = int(f[1]), int(f[2]), int(f[3])
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        blob = torch.randint(0, 256, (N * (K // 256), 144), dtype=torch.uint8, device=dev, generator=g)
+        blob[:, 0:2] = torch.tensor([0.002], dtype=torch.float16).view(torch.uint8).to(dev)
+        blob[:, 2:4] = blob[:, 0:2]
+        tile, S, B = hq.q4_k_to_tile(blob.reshape(-1), K, N)
+        A = torch.randn((M, K), device=dev, generator=g).half()
+        for _ in range(args.steps):
+            y = hq.gemm(A, tile, S, N=N, group=32, bias=B)
+        torch.cuda.synchronize()
+        hq.check_device_error()
+        print(json.dumps({"case": args.case, "checksum": float(y.float().abs().sum())}))
+        return 0
     K, N, M = int(f[0]), int(f[1]), int(f[2])
     dt = f[3] if len(f) > 3 else "f16"
     wfmt = _lib.HQ_WFMT_TILE_T2 if len(f) > 4 and f[4] == "t2" else _lib.HQ_WFMT_TILE_U4
@@ -841,7 +856,8 @@ def main():
                     help="reference arm: skip timing the reference's CUDA kernels on the GPU")
     ap.add_argument("--case", default=None,
                     help="profiling aid: 'K,N,M[,f16|bf16[,u4|t2]]' runs that one hq_gemm `--steps` times and exits; "
-                         "'tq1,K,N' runs hq_tq1_0_gemv, 'proj,TYPE,K,N' hq_output_projection instead")
+                         "'tq1,K,N' runs hq_tq1_0_gemv, 'proj,TYPE,K,N' hq_output_projection, 'q4k,K,N,M' the "
+                         "group-32 GEMM on converted Q4_K blocks instead")
     ap.add_argument("--stack-layers", type=int, default=64)
     ap.add_argument("--stack-steps", type=int, default=3)
     ap.add_argument("--stack-comm", default="hq", choices=["hq", "nccl"], help="collective of the TP stack")
