@@ -251,7 +251,7 @@ HQ_API hq_status hq_q4_k_to_tile_host(const void* w_q4k, void* tile, float* scal
  * (marlin_gemm.cu:327-377, 603-617); any M (the reference's acc[8] stops at 8).
  * The int32 sums are exact and rounded once (the reference rounds an fp32
  * running sum per quad): results within 1e-5 of max|Y| of the reference's.
- * N % 4 == 0, K <= 65536, W 4-byte aligned; Y is used as int32 scratch first.
+ * N % 4 == 0, K <= 65536, W 4-byte aligned.  One launch per 8 rows of X.
  */
 HQ_API hq_status hq_w8_gemm(const float* X, const int8_t* W, const float* scales, float* Y,
                             int M, int K, int N, hq_stream_t stream);
