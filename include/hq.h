@@ -124,12 +124,14 @@ HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t
  *   s_dtype: HQ_F16 | HQ_BF16 | HQ_F32; bias is always f32.  Combinations
  *            (activations, scales): (f16, f16), (bf16, bf16), (f16 | bf16 | f32,
  *            f32), (f32, f16); a bias goes with f32 scales and f16 / f32
- *            activations.  Ternary weights: (f16, f16), (bf16, bf16).
+ *            activations.  Group 32: f32 scales only.  Ternary weights:
+ *            (f16, f16), (bf16, bf16).
  *   c_dtype: HQ_F16 | HQ_BF16 | HQ_F32: the activation type, or f32
- *   wfmt:    HQ_WFMT_TILE_U4 / HQ_WFMT_TILE_T2 run directly.  LINEAR_U4,
- *            MARLIN_QUAD and LINEAR_T2 are accepted for drop-in use and are
- *            re-tiled into the workspace first (one extra pass over the
- *            weights); hq_gemm_workspace_size accounts for it.
+ *   wfmt:    HQ_WFMT_TILE_U4 (groups that are multiples of 64),
+ *            HQ_WFMT_TILE_U4_K32 (group 32) and HQ_WFMT_TILE_T2 run directly.
+ *            LINEAR_U4, MARLIN_QUAD and LINEAR_T2 are accepted for drop-in use
+ *            and are re-tiled into the workspace first (one extra pass over
+ *            the weights); hq_gemm_workspace_size accounts for it.
  * M <= 16 runs the HBM-streaming decode kernel; larger M runs the tcgen05
  * tensor-core kernel, which rounds each dequantised weight to the 16-bit
  * activation type (with f32 scales: u * s + b formed in fp32, rounded once).
