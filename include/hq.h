@@ -125,7 +125,9 @@ HQ_API hq_status hq_workspace_init(void* workspace, size_t ws_bytes, hq_stream_t
  *            (activations, scales): (f16, f16), (bf16, bf16), (f16 | bf16 | f32,
  *            f32), (f32, f16); a bias goes with f32 scales and f16 / f32
  *            activations.  Group 32: f32 scales only.  Ternary weights:
- *            (f16, f16), (bf16, bf16).
+ *            (f16, f16), (bf16, bf16), (f32, f16) (the last with f32 output:
+ *            TQ1_0 layers converted by hq_tq1_0_to_tile_t2, fp32 x as in
+ *            kernel_gemv_tq1_0).
  *   c_dtype: HQ_F16 | HQ_BF16 | HQ_F32: the activation type, or f32
  *   wfmt:    HQ_WFMT_TILE_U4 (groups that are multiples of 64),
  *            HQ_WFMT_TILE_U4_K32 (group 32) and HQ_WFMT_TILE_T2 run directly.

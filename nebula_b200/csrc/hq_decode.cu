@@ -670,7 +670,7 @@ KernelInfo pick_out(DType c) {
 
 // Supported (activation, scale, bias) combinations.  int4: (f16,f16), (bf16,bf16),
 // (f16|bf16, f32), (f32, f32) with or without bias for f16/f32 activations, and
-// (f32, f16).  Ternary: (f16,f16), (bf16,bf16).  Group 32 (int4, f32 scales):
+// (f32, f16).  Ternary: (f16,f16), (bf16,bf16), (f32, f16).  Group 32 (int4, f32 scales):
 // f16 / f32 activations with or without bias, bf16 without.
 template <int WBITS, int MT>
 KernelInfo pick(const GemmArgs& a) {
@@ -692,6 +692,12 @@ KernelInfo pick(const GemmArgs& a) {
         return pick_out<WBITS, MT, __half, __half, false>(a.c_dtype);
     if (a.a_dtype == DType::BF16 && a.s_dtype == DType::BF16 && !bias)
         return pick_out<WBITS, MT, __nv_bfloat16, __nv_bfloat16, false>(a.c_dtype);
+    if constexpr (WBITS == 2) {
+        // fp32 activations (two fp16 terms) on ternary weights with fp16 scales:
+        // TQ1_0 layers converted at load (hq_tq1_0_to_tile_t2) with the reference's fp32 x
+        if (a.a_dtype == DType::F32 && a.s_dtype == DType::F16 && !bias)
+            return pick_out<WBITS, MT, float, __half, false>(a.c_dtype);
+    }
     if constexpr (WBITS == 4) {
         if (a.a_dtype == DType::F16 && a.s_dtype == DType::F32)
             return bias ? pick_out<WBITS, MT, __half, float, true>(a.c_dtype)
@@ -788,9 +794,9 @@ cudaError_t launch_decode(const GemmArgs& a) {
     // twice the MMAs.  Smaller fp32 layers stay here (QKV 17.8 us against 19.4).
     const TileGeom tg(a.K, a.N, a.wbits);
     const bool g64 = a.group % kBlockK == 0;  // group 32 runs only here
-    const bool i8_shape = g64 && a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
-                          : a.wbits == 2          ? tg.NSG >= HQ_DECODE_I8_MIN_NSG_T2
-                                                  : tg.NSG >= HQ_DECODE_I8_MIN_NSG;
+    const bool i8_shape = g64 && (a.a_dtype == DType::F32 ? tg.units() >= HQ_DECODE_I8_MIN_UNITS_F32
+                                  : a.wbits == 2          ? tg.NSG >= HQ_DECODE_I8_MIN_NSG_T2
+                                                          : tg.NSG >= HQ_DECODE_I8_MIN_NSG);
     if (a.M <= HQ_DECODE_I8_MAX_M && i8_shape && decode_i8_supported(a)) return launch_decode_i8(a, g_early_weights);
     // M > 8 on wide layers (>= 128 strip groups) runs on tcgen05: the mma.sync
     // kernel needs two token tiles there and the tensor-memory kernel's cost does

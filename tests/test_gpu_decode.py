@@ -285,6 +285,25 @@ def test_tq1_0_to_tile_t2_then_gemm(K, N):
     assert o.max_rel_err(y2.cpu().numpy()[0], ref2) <= TOL["f16"]
 
 
+@pytest.mark.parametrize("K,N", [(512, 48), (5120, 7168), (17408, 5120)])
+@pytest.mark.parametrize("M", [1, 3, 16])
+def test_tq1_0_layers_at_load_with_fp32_x(K, N, M):
+    """TQ1_0 layers converted once at load (hq_tq1_0_to_tile_t2), then hq_gemm with the reference's
+    fp32 x (two fp16 terms on the split-K kernel) and fp32 output: against the oracle's
+    restatement of kernel_gemv_tq1_0, row by row, within 1e-5 of max|out|."""
+    rng = np.random.default_rng(K + N + M)
+    t = rng.integers(-1, 2, size=(N, K), dtype=np.int8)
+    d = rng.uniform(0.01, 0.05, size=(N, K // 256)).astype(np.float16).view(np.uint16)
+    d[1, 0] = 0x7E00  # NaN block scale: skipped, as in the reference
+    blob = o.pack_tq1_0(t, d)
+    tile, scales = hq.tq1_0_to_tile_t2(cuda(blob, None), K, N)
+    X = (rng.standard_normal((M, K)) * 0.5).astype(np.float32)
+    Y = hq.gemm(cuda(X, "f32"), tile, scales, N=N, group=128, wfmt=_lib.HQ_WFMT_TILE_T2,
+                out_dtype=torch.float32).cpu().numpy()
+    for m in range(M):
+        assert o.max_rel_err(Y[m], o.gemv_tq1_0(X[m], blob, K, N)) <= 1e-5
+
+
 @pytest.mark.parametrize("K,N", [(1024, 1), (1024, 45), (2048, 100), (768, 37), (4096, 4097)])
 def test_tq1_0_gemv_edge_shapes(K, N):
     """Tensor-core path (K % 1024 == 0) with ragged row counts, and the row-per-warp path (K = 768);
