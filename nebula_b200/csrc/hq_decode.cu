@@ -50,7 +50,7 @@ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
 // Shared-memory layout of one pipeline stage.  kG32: scale groups of 32 k, so
 // each 64-k block has two scale (and bias) rows.
-template <int WBITS, typename AT, typename ST, bool kBias, bool kG32>
+template <int WBITS, typename AT, typename ST, bool kBias, bool kG32, int kNStages = 4>
 struct Stage {
     static constexpr int kCB = WBITS == 4 ? 512 : 256;
     static constexpr int kWBytes = kUPS * kGroupStrips * kCB;  // weights of a full group
@@ -69,7 +69,7 @@ struct Stage {
     static constexpr int kS = kX + kUPS * kXUnit;
     static constexpr int kB = kS + kUPS * kSUnit;
     static constexpr int kBytes = align_up(kB + kUPS * kBUnit, 1024);
-    static constexpr int kStages = 4;
+    static constexpr int kStages = kNStages;
     static constexpr int kSmem = kStages * kBytes + 1024 /* base alignment slack */ + 2 * kStages * 8;
 };
 
@@ -218,9 +218,9 @@ __device__ __forceinline__ float lds_scale(const uint8_t* sp) {
     return to_f32(*reinterpret_cast<const ST*>(sp));
 }
 
-template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32>
+template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32, int kNStages = 4>
 __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using L = Stage<WBITS, AT, ST, kBias, kG32>;
+    using L = Stage<WBITS, AT, ST, kBias, kG32, kNStages>;
     constexpr bool kSplit = std::is_same<AT, float>::value;
     constexpr bool kBF16 = ComputeType<AT>::bf16;  // float activations compute in fp16
     constexpr int kCB = L::kCB;
@@ -649,23 +649,34 @@ struct KernelInfo {
     bool x_tma = false;
 };
 
-template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32>
+template <int WBITS, int MT, typename AT, typename ST, typename OT, bool kBias, bool kG32, int kNStages>
 KernelInfo kernel_info() {
-    using L = Stage<WBITS, AT, ST, kBias, kG32>;
-    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias, kG32>, L::kSmem, L::kXTma};
+    using L = Stage<WBITS, AT, ST, kBias, kG32, kNStages>;
+    return {decode_kernel<WBITS, MT, AT, ST, OT, kBias, kG32, kNStages>, L::kSmem, L::kXTma};
 }
 
 // Output dtype: the activation's own 16-bit type or f32 (f32 activations: f32 out).
-template <int WBITS, int MT, typename AT, typename ST, bool kBias, bool kG32 = false>
+template <int WBITS, int MT, typename AT, typename ST, bool kBias, bool kG32 = false, int kNStages = 4>
 KernelInfo pick_out(DType c) {
-    if (c == DType::F32) return kernel_info<WBITS, MT, AT, ST, float, kBias, kG32>();
+    if (c == DType::F32) return kernel_info<WBITS, MT, AT, ST, float, kBias, kG32, kNStages>();
     if constexpr (std::is_same<AT, __half>::value) {
-        if (c == DType::F16) return kernel_info<WBITS, MT, AT, ST, __half, kBias, kG32>();
+        if (c == DType::F16) return kernel_info<WBITS, MT, AT, ST, __half, kBias, kG32, kNStages>();
     }
     if constexpr (std::is_same<AT, __nv_bfloat16>::value) {
-        if (c == DType::BF16) return kernel_info<WBITS, MT, AT, ST, __nv_bfloat16, kBias, kG32>();
+        if (c == DType::BF16) return kernel_info<WBITS, MT, AT, ST, __nv_bfloat16, kBias, kG32, kNStages>();
     }
     return {};
+}
+
+// Group 32 at M <= 8: three stages let four CTAs share an SM (the two extra scale and
+// bias rows make four stages too large for that), which pays on layers of >= 56 strip
+// groups (Q4_K at M = 1: gate_up 46.4 -> 34.5 us, QKV 15.8 -> 11.8) and loses on
+// narrower ones, whose clusters of 8-12 CTAs per strip group need the deeper ring
+// (O 9.9 -> 11.4 us).
+template <int MT, typename AT, bool kBias>
+KernelInfo pick_g32(const GemmArgs& a) {
+    if (MT == 1 && TileGeom(a.K, a.N, 4).NSG >= 56) return pick_out<4, MT, AT, float, kBias, true, 3>(a.c_dtype);
+    return pick_out<4, MT, AT, float, kBias, true, 4>(a.c_dtype);
 }
 
 // Supported (activation, scale, bias) combinations.  int4: (f16,f16), (bf16,bf16),
@@ -678,13 +689,9 @@ KernelInfo pick(const GemmArgs& a) {
     if (a.group % kBlockK) {
         if constexpr (WBITS == 4) {
             if (a.group != 32 || a.s_dtype != DType::F32) return {};
-            if (a.a_dtype == DType::F16)
-                return bias ? pick_out<4, MT, __half, float, true, true>(a.c_dtype)
-                            : pick_out<4, MT, __half, float, false, true>(a.c_dtype);
-            if (a.a_dtype == DType::BF16 && !bias) return pick_out<4, MT, __nv_bfloat16, float, false, true>(a.c_dtype);
-            if (a.a_dtype == DType::F32)
-                return bias ? pick_out<4, MT, float, float, true, true>(a.c_dtype)
-                            : pick_out<4, MT, float, float, false, true>(a.c_dtype);
+            if (a.a_dtype == DType::F16) return bias ? pick_g32<MT, __half, true>(a) : pick_g32<MT, __half, false>(a);
+            if (a.a_dtype == DType::BF16 && !bias) return pick_g32<MT, __nv_bfloat16, false>(a);
+            if (a.a_dtype == DType::F32) return bias ? pick_g32<MT, float, true>(a) : pick_g32<MT, float, false>(a);
         }
         return {};
     }

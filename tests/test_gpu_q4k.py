@@ -227,3 +227,19 @@ def test_device_repack_k32(K, N):
         assert np.array_equal(t.cpu().numpy(), want)
     back = hq.repack(dev_u8(want), hq.HQ_WFMT_TILE_U4_K32, hq.HQ_WFMT_LINEAR_U4, K, N)
     assert np.array_equal(back.cpu().numpy().view(np.uint32).reshape(lin.shape), lin)
+
+
+@pytest.mark.parametrize("M", [1, 5, 8])
+@pytest.mark.parametrize("a_dtype,with_bias", [("f16", True), ("f32", True), ("bf16", False), ("f16", False)])
+def test_group32_wide_layer(M, a_dtype, with_bias):
+    """Group 32 on a layer of >= 56 strip groups at M <= 8 (N = 8192: the three-stage ring)."""
+    K, N = 512, 8192
+    rng = np.random.default_rng(M + N)
+    A, q, _ = o.gen_int4_case(M, K, N, group=32, seed=M + 17, a_dtype=a_dtype)
+    S = (0.005 + rng.random((K // 32, N)) * 0.015).astype(np.float32)
+    B = (-8.0 * S + 0.01 * rng.standard_normal(S.shape)).astype(np.float32) if with_bias else None
+    ref = o.w4_gemm(A, o.pack_linear_u4(q), S, B, group=32)
+    y = hq.gemm(torch.from_numpy(A).to("cuda:0").to(TDT[a_dtype]), dev_u8(o.pack_tile_k32(q)),
+                torch.from_numpy(S).to("cuda:0"), N=N, group=32,
+                bias=torch.from_numpy(B).to("cuda:0") if with_bias else None, out_dtype=torch.float32)
+    assert o.max_rel_err(y.cpu().numpy(), ref) <= 1e-4
