@@ -675,8 +675,22 @@ KernelInfo pick_out(DType c) {
 // (O 9.9 -> 11.4 us).
 template <int MT, typename AT, bool kBias>
 KernelInfo pick_g32(const GemmArgs& a) {
-    if (MT == 1 && TileGeom(a.K, a.N, 4).NSG >= 56) return pick_out<4, MT, AT, float, kBias, true, 3>(a.c_dtype);
+    if constexpr (MT == 1) {
+        if (TileGeom(a.K, a.N, 4).NSG >= 56) return pick_out<4, MT, AT, float, kBias, true, 3>(a.c_dtype);
+    }
     return pick_out<4, MT, AT, float, kBias, true, 4>(a.c_dtype);
+}
+
+// fp32 activations (group >= 64) at M <= 8: their padded activation rows make a stage
+// ~19 KB, so four stages hold two or three CTAs per SM.  Three stages (one CTA more)
+// pay on layers of < 56 strip groups (the reference's fp32 form, O at M = 1: 16.3 ->
+// 11.5 us; down at M = 8: 39.1 -> 27.0) and lose on wider ones (QKV 16.7 -> 19.4).
+template <int MT, typename ST, bool kBias>
+KernelInfo pick_f32(const GemmArgs& a) {
+    if constexpr (MT == 1) {
+        if (TileGeom(a.K, a.N, 4).NSG < 56) return pick_out<4, MT, float, ST, kBias, false, 3>(a.c_dtype);
+    }
+    return pick_out<4, MT, float, ST, kBias, false, 4>(a.c_dtype);
 }
 
 // Supported (activation, scale, bias) combinations.  int4: (f16,f16), (bf16,bf16),
@@ -712,10 +726,8 @@ KernelInfo pick(const GemmArgs& a) {
         if (a.a_dtype == DType::BF16 && a.s_dtype == DType::F32 && !bias)
             return pick_out<WBITS, MT, __nv_bfloat16, float, false>(a.c_dtype);
         if (a.a_dtype == DType::F32 && a.s_dtype == DType::F32)
-            return bias ? pick_out<WBITS, MT, float, float, true>(a.c_dtype)
-                        : pick_out<WBITS, MT, float, float, false>(a.c_dtype);
-        if (a.a_dtype == DType::F32 && a.s_dtype == DType::F16 && !bias)
-            return pick_out<WBITS, MT, float, __half, false>(a.c_dtype);
+            return bias ? pick_f32<MT, float, true>(a) : pick_f32<MT, float, false>(a);
+        if (a.a_dtype == DType::F32 && a.s_dtype == DType::F16 && !bias) return pick_f32<MT, __half, false>(a);
     }
     return {};
 }
