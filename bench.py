@@ -494,7 +494,7 @@ def w8_sweep(torch, L, _lib, dev, stream, peaks, args):
                      "GBps": round(K * N / (ms / 1e3) / 1e9, 1)})
         del W
     return {"metric": "W8A8 GEMM weight GB/s (forward_cutlass_int8)", "per_gemm": rows,
-            "timing": "CUDA events around 10 calls (memset + 2 kernels each) after 3 warm-up, 2 weight copies"}
+            "timing": "CUDA events around 10 calls (one cluster kernel each) after 3 warm-up, 2 weight copies"}
 
 
 def _ternary_tile(torch, nbytes, dev, g):
