@@ -206,7 +206,13 @@ __device__ __forceinline__ void load8(const AT* p, float (&f)[8]) {
 // holds the rest, x - x_hi (exact in fp32, |x - x_hi| <= 2^-s-1), in steps of
 // 2^-(s+15).  Both slots of a token land in the same lanes (tiles j and
 // j + NT/2), whose sums the GEMM adds before storing.
-template <typename AT, bool RES>
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+template <typename AT, bool RES, bool T2 = false>
 __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restrict__ A, int M, int K, int group,
                                                               int slots, int8_t* __restrict__ pieces,
                                                               float* __restrict__ xscale, float* __restrict__ xsum,
@@ -271,11 +277,12 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
             for (int i = 0; i < 8; ++i) xf[i] = 0;
         }
         uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-        // byte j of word A holds element {0,2,1,3}[j], of word B element {4,6,5,7}[j]
+        // int4: byte j of word A holds element {0,2,1,3}[j], of word B element {4,6,5,7}[j];
+        // ternary: the elements in natural order (0..3, 4..7), interleaved with the other octet below
         constexpr int kOrder[8] = {0, 2, 1, 3, 4, 6, 5, 7};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int v = xf[kOrder[j]];
+            const int v = xf[T2 ? j : kOrder[j]];
             const int h = (v + 128) >> 8;
             const int l = v - (h << 8);
             hw[j >> 2] |= (uint32_t)(h & 0xFF) << (8 * (j & 3));
@@ -286,10 +293,32 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
         int8_t* tile = pieces + (size_t)kb * slots * 128;
         uint32_t* ph = reinterpret_cast<uint32_t*>(tile + ((m * 2 + 0) * 4 + t) * 16);
         uint32_t* pl = reinterpret_cast<uint32_t*>(tile + ((m * 2 + 1) * 4 + t) * 16);
-        ph[hh] = hw[0];
-        ph[2 + hh] = hw[1];
-        pl[hh] = lw[0];
-        pl[2 + hh] = lw[1];
+        if constexpr (T2) {
+            // The 16 bytes of lane t are elements {0,8,1,9}, {2,10,3,11}, {4,12,5,13},
+            // {6,14,7,15} of its 16 k: the order in which (w >> 2s) & 0x03030303 takes
+            // codes out of a TILE_T2 word, so the kernel needs no byte permutes.  The
+            // other octet of the 16 k is in the neighbouring lane (o ^ 1, as group % 64
+            // == 0): the low-k lane writes words 0-1, the high-k lane words 2-3.
+            const unsigned act = __activemask();
+            const uint32_t rh = __shfl_xor_sync(act, hh ? hw[0] : hw[1], 1);
+            const uint32_t rl = __shfl_xor_sync(act, hh ? lw[0] : lw[1], 1);
+            if (!hh) {
+                ph[0] = prmt(hw[0], rh, 0x5140u);
+                ph[1] = prmt(hw[0], rh, 0x7362u);
+                pl[0] = prmt(lw[0], rl, 0x5140u);
+                pl[1] = prmt(lw[0], rl, 0x7362u);
+            } else {
+                ph[2] = prmt(rh, hw[1], 0x5140u);
+                ph[3] = prmt(rh, hw[1], 0x7362u);
+                pl[2] = prmt(rl, lw[1], 0x5140u);
+                pl[3] = prmt(rl, lw[1], 0x7362u);
+            }
+        } else {
+            ph[hh] = hw[0];
+            ph[2 + hh] = hw[1];
+            pl[hh] = lw[0];
+            pl[2 + hh] = lw[1];
+        }
         if (xkb) {  // ternary: sum of the fixed-point x over each k-block (8 octets = 8 lanes)
             int sum8 = 0;
 #pragma unroll
@@ -304,23 +333,16 @@ __global__ void __launch_bounds__(kPrepThreads) x_prep_kernel(const AT* __restri
 }
 
 // Ternary codes c = q + 1 (2 bits, TILE_T2 word of 16 consecutive k of one
-// column, code e at field (e >> 1) + 8 (e & 1)) as u8 MMA operands in the k-slot
-// order of the int4 path (so the same activation pieces serve both):
-// MMA 0 takes e = {0,2,1,3} (slots 4t..) and 8 + {0,2,1,3} (slots 16 + 4t..),
-// MMA 1 takes e = {4,6,5,7} and 8 + {4,6,5,7}.  Four masks select fields
-// (f, f + 4, f + 8, f + 12) into bytes, four byte permutes pick the pairs.
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
+// column, code e at field (e >> 1) + 8 (e & 1)) as u8 MMA operands: field class
+// s (fields s, s + 4, s + 8, s + 12, one per byte) is (w >> 2s) & 0x03030303,
+// i.e. codes e = {0,8,1,9} (s = 0), {2,10,3,11}, {4,12,5,13}, {6,14,7,15}; the
+// prep kernel writes the ternary activation pieces in that order, so MMA 0
+// takes classes 0 (slots 4t..) and 1 (slots 16 + 4t..) and MMA 1 classes 2, 3.
 __device__ __forceinline__ void t2_operands(uint32_t w, uint32_t& m0a, uint32_t& m0b, uint32_t& m1a, uint32_t& m1b) {
-    const uint32_t f0 = w & 0x03030303u, f1 = (w >> 2) & 0x03030303u;
-    const uint32_t f2 = (w >> 4) & 0x03030303u, f3 = (w >> 6) & 0x03030303u;
-    m0a = prmt(f0, f1, 0x6240u);
-    m0b = prmt(f0, f1, 0x7351u);
-    m1a = prmt(f2, f3, 0x6240u);
-    m1b = prmt(f2, f3, 0x7351u);
+    m0a = w & 0x03030303u;
+    m0b = (w >> 2) & 0x03030303u;
+    m1a = (w >> 4) & 0x03030303u;
+    m1b = (w >> 6) & 0x03030303u;
 }
 // D (16x8 s32) += A (16x32 u8) x B (32x8 s8).
 __device__ __forceinline__ void imma_16832_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -820,12 +842,15 @@ cudaError_t launch_decode_i8(const GemmArgs& a, bool early_weights) {
     pc.stream = a.stream;
     pc.attrs = pdl;
     pc.numAttrs = 1;
+    const bool t2 = a.wbits == 2;
     if (a.a_dtype == DType::F16)
-        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__half, false>, static_cast<const __half*>(a.A), a.M, a.K, a.group,
-                               NT * kTokTile, pieces, xscale, xsum, xkb);
+        e = cudaLaunchKernelEx(&pc, t2 ? x_prep_kernel<__half, false, true> : x_prep_kernel<__half, false>,
+                               static_cast<const __half*>(a.A), a.M, a.K, a.group, NT * kTokTile, pieces, xscale,
+                               xsum, xkb);
     else if (a.a_dtype == DType::BF16)
-        e = cudaLaunchKernelEx(&pc, x_prep_kernel<__nv_bfloat16, false>, static_cast<const __nv_bfloat16*>(a.A), a.M,
-                               a.K, a.group, NT * kTokTile, pieces, xscale, xsum, xkb);
+        e = cudaLaunchKernelEx(&pc, t2 ? x_prep_kernel<__nv_bfloat16, false, true> : x_prep_kernel<__nv_bfloat16, false>,
+                               static_cast<const __nv_bfloat16*>(a.A), a.M, a.K, a.group, NT * kTokTile, pieces,
+                               xscale, xsum, xkb);
     else
         e = cudaLaunchKernelEx(&pc, x_prep_kernel<float, true>, static_cast<const float*>(a.A), a.M, a.K, a.group,
                                NT * kTokTile, pieces, xscale, xsum, static_cast<int*>(nullptr));

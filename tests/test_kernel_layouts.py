@@ -251,16 +251,28 @@ def _prmt(a, b, sel):
 
 
 def _t2_operands(w):
-    """hq_decode_i8.cu t2_operands: one TILE_T2 word -> (MMA 0 slots 4t.., MMA 0 slots 16+4t.., MMA 1 ...)."""
-    f0, f1 = w & 0x03030303, (w >> 2) & 0x03030303
-    f2, f3 = (w >> 4) & 0x03030303, (w >> 6) & 0x03030303
-    return _prmt(f0, f1, 0x6240), _prmt(f0, f1, 0x7351), _prmt(f2, f3, 0x6240), _prmt(f2, f3, 0x7351)
+    """hq_decode_i8.cu t2_operands: one TILE_T2 word -> its four field classes (MMA 0 slots 4t..,
+    MMA 0 slots 16+4t.., MMA 1 ...), one mask each."""
+    return w & 0x03030303, (w >> 2) & 0x03030303, (w >> 4) & 0x03030303, (w >> 6) & 0x03030303
+
+
+# Ternary activation pieces (x_prep_kernel<..., T2 = true>): byte j of lane t's 16 bytes holds element
+# _T2_PIECE_POS[j] of its 16 k, the order of the field classes above.
+_T2_PIECE_POS = [0, 8, 1, 9, 2, 10, 3, 11, 4, 12, 5, 13, 6, 14, 7, 15]
+
+
+def _t2_prep_words(h_oct0, h_oct1):
+    """The prep kernel's assembly of one lane's four words from its two octets' natural-order bytes
+    (prmt 0x5140 / 0x7362 across the pair of neighbouring prep lanes)."""
+    w = lambda v: int.from_bytes(bytes(int(x) & 0xFF for x in v), "little")  # noqa: E731
+    e0a, e1a, e0b, e1b = w(h_oct0[0:4]), w(h_oct0[4:8]), w(h_oct1[0:4]), w(h_oct1[4:8])
+    return [_prmt(e0a, e0b, 0x5140), _prmt(e0a, e0b, 0x7362), _prmt(e1a, e1b, 0x5140), _prmt(e1a, e1b, 0x7362)]
 
 
 @pytest.mark.parametrize("seed", range(3))
 def test_int8_decode_ternary_fragments_give_q_dot_x(seed):
-    """The integer decode kernel's ternary operands: codes c = q + 1 as u8 in the int4 path's k-slot
-    order, so that with the same activation pieces sum c x - sum x = sum q x (one 64-k block)."""
+    """The integer decode kernel's ternary operands: codes c = q + 1 as u8 field classes, with the
+    ternary activation pieces in the matching order, give sum c x - sum x = sum q x (one 64-k block)."""
     rng = np.random.default_rng(100 + seed)
     K, N, M = 64, 16, 4
     t = rng.integers(-1, 2, size=(K, N), dtype=np.int8)
@@ -272,7 +284,10 @@ def test_int8_decode_ternary_fragments_give_q_dot_x(seed):
     for m in range(M):
         for p, arr in enumerate((h, l)):
             for tt in range(4):
-                pieces[(m * 2 + p) * 4 + tt] = [arr[m, 16 * tt + _PIECE_POS[j]] for j in range(16)]
+                pieces[(m * 2 + p) * 4 + tt] = [arr[m, 16 * tt + _T2_PIECE_POS[j]] for j in range(16)]
+                # the prep kernel's two-lane assembly gives the same bytes
+                words = _t2_prep_words(arr[m, 16 * tt:16 * tt + 8], arr[m, 16 * tt + 8:16 * tt + 16])
+                assert np.array_equal(np.array(words, np.uint32).view(np.int8), pieces[(m * 2 + p) * 4 + tt])
     xbytes = pieces.reshape(-1).view(np.uint32).reshape(32, 4)
     a0, a1 = [], []
     for lane in range(32):
